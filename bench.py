@@ -1,0 +1,468 @@
+#!/usr/bin/env python3
+"""Benchmark of the tmnn hot path on B200 (one JSON line on rank 0).
+
+Workload (default): BASELINE configs[1], the 3D SDF fit -- 2^18 points per
+step per GPU uniform in [-1,1]^3, target = SDF of a seeded union of 8 spheres
+(radii U[0.1, 0.4]); HashGrid 16 levels x 2 fp16 features, log2T 19, base
+16, scale 1.447; FullyFusedMLP 64 wide, 1 hidden layer, 1 output; L1 loss;
+fused Adam lr 1e-2.  A "step" is one training step (Morton sort, fused
+forward/backward/scatter, [gradient allreduce], Adam) over one batch.
+
+  value  whole-job training throughput in 2^18-point steps per second
+         (= samples/s / 2^18), inputs resident in HBM, device-timed with CUDA
+         events on the library's stream, max over ranks.
+  e2e    the same through the public API with pinned HOST inputs: the
+         host->device copy of every batch and the loss read-back are timed.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+Multi-GPU: torchrun --nproc-per-node N bench.py --gpus N (data parallel,
+2^18 points per GPU, one NCCL allreduce of the gradients per step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tiny-metal-nn_b200"))
+
+WORKLOADS = {
+    # BASELINE configs[1]
+    "sdf3d": dict(L=16, F=2, log2T=19, d=3, base=16.0, scale=1.447, W=64, H=1,
+                  O=1, loss="L1", lr=1e-2, batch=1 << 18, table="F16",
+                  desc="3D SDF fit, batch 2^18/GPU, HashGrid 16x2 fp16 "
+                       "T=2^19, MLP 64x1 -> 1, L1, Adam lr 1e-2"),
+    # BASELINE configs[0] shape at the north-star batch
+    "image": dict(L=16, F=2, log2T=15, d=3, base=16.0, scale=1.5, W=64, H=2,
+                  O=3, loss="L2", lr=1e-2, batch=1 << 18, table="F32",
+                  desc="2D image fit (x,y,0), batch 2^18/GPU, HashGrid 16x2 "
+                       "T=2^15, MLP 64x2 -> 3, L2, Adam lr 1e-2"),
+    # BASELINE configs[4]
+    "field4d": dict(L=16, F=2, log2T=22, d=4, base=8.0, scale=1.5, W=64, H=2,
+                    O=4, loss="L2", lr=1e-2, batch=1 << 18, table="F16",
+                    desc="4D field, batch 2^18/GPU, HashGrid 16x2 fp16 "
+                         "T=2^22, MLP 64x2 -> 4, L2, Adam lr 1e-2"),
+}
+
+# DRAM bytes per fwd/bwd launch from the committed ncu capture of the
+# dominant kernel (profiles/), per workload and family; None until captured.
+NCU_TRAFFIC_PER_SAMPLE = {}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_config(w, family, grad, morton):
+    return {
+        "encoding": {"otype": "HashGrid", "n_levels": w["L"],
+                     "n_features_per_level": w["F"],
+                     "log2_hashmap_size": w["log2T"],
+                     "base_resolution": w["base"],
+                     "per_level_scale": w["scale"]},
+        "network": {"otype": "FullyFusedMLP", "n_neurons": w["W"],
+                    "n_hidden_layers": w["H"]},
+        "loss": {"otype": w["loss"]},
+        "optimizer": {"otype": "Adam", "learning_rate": w["lr"]},
+        "b200": {"family": family, "hash_grad_format": grad,
+                 "table_dtype": w["table"], "morton_sort": morton},
+    }
+
+
+def sphere_params(seed=1234):
+    rng = np.random.default_rng(seed)
+    centers = rng.uniform(-0.6, 0.6, (8, 3)).astype(np.float32)
+    radii = rng.uniform(0.1, 0.4, 8).astype(np.float32)
+    return centers, radii
+
+
+def make_batch_np(w, n, seed):
+    """Seeded synthetic batch (positions, targets) for workload w."""
+    rng = np.random.default_rng(seed)
+    d, O = w["d"], w["O"]
+    if d == 3 and O == 1:
+        pos = rng.uniform(-1, 1, (n, 3)).astype(np.float32)
+        c, r = sphere_params()
+        dist = np.linalg.norm(pos[:, None, :] - c[None], axis=2) - r[None]
+        tgt = dist.min(axis=1, keepdims=True).astype(np.float32)
+    elif d == 3:
+        # image: (x, y, 0) lift, target = RGB of a sum of 32 sinusoids
+        xy = rng.uniform(0, 1, (n, 2)).astype(np.float32)
+        pos = np.concatenate([xy, np.zeros((n, 1), np.float32)], 1)
+        fr = np.random.default_rng(77).normal(size=(32, 2, 3)) * 6
+        ph = np.random.default_rng(78).uniform(0, 6.28, (32, 3))
+        tgt = np.zeros((n, O), np.float32)
+        for k in range(32):
+            tgt += np.sin(xy @ fr[k] + ph[k]).astype(np.float32) / 32
+    else:
+        pos = rng.uniform(0, 1, (n, 4)).astype(np.float32)
+        g = np.random.default_rng(99)
+        mu = g.uniform(0, 1, (64, 4))
+        tgt = np.zeros((n, O), np.float32)
+        for k in range(64):
+            tgt[:, k % O] += np.exp(-((pos - mu[k]) ** 2).sum(1) * 20).astype(np.float32)
+    return pos, tgt
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i in range(4)
+                          if r[i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(w, seconds=12.0):
+    """The CPU oracle (the reference's math restated in C, OpenMP over every
+    host core) on a bounded sample of the same workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    s = o.make_spec(L=w["L"], F=w["F"], log2T=w["log2T"], d=w["d"], W=w["W"],
+                    H=w["H"], O=w["O"], loss=w["loss"], base=w["base"],
+                    scale=w["scale"], grad_mode=o.GRAD_FLOAT)
+    hw, mw = o.init_weights(s)
+    tr = o.OracleTrainer(s, hw, mw, lr_hash=w["lr"], lr_mlp=w["lr"],
+                         nthreads=0)
+    n = 1 << 14
+    pos, tgt = make_batch_np(w, n, 7)
+    tr.training_step(pos, tgt)  # warm-up
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        tr.training_step(pos, tgt)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > seconds or steps >= 50:
+            break
+    sps = steps * n / el
+    cores = os.cpu_count()
+    return {"value": sps / w["batch"], "unit": "steps/s (2^18-point batches)",
+            "cores": cores, "kind": "port",
+            "sample": f"{steps} oracle training steps of {n} points (Morton sort, "
+                      f"fwd/bwd, Adam over the full table) on {cores} threads, "
+                      f"{el:.1f} s; value = samples/s / 2^18",
+            "samples_per_s": sps}
+
+
+def run_reference(args, w):
+    """Reference arm: the reference's own code compiled here (oracle/_ref:
+    its generated scalar train kernel run as C++ through the Metal shim, its
+    Morton sort, its sparse/dense Adam kernels), host cores only."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref_oracle as ro
+    tag = "bench_" + args.workload
+    if not ro.available(tag) or not ro.available("static"):
+        return {"impl": "reference",
+                "unavailable": f"oracle/_ref/libtmnn_ref_{tag}.so not built "
+                               "(python oracle/ref_build.py with the reference "
+                               "sources)"}
+    sp = ro.spec_tuple(tag)
+    L, F, log2T, d, W, H, O = sp[:7]
+    T = 1 << log2T
+    rng = np.random.default_rng(3)
+    table = rng.uniform(-1e-4, 1e-4, L * T * F).astype(np.float32)
+    In = L * F
+    n_mlp = In * W + W + (H - 1) * (W * W + W) + W * O + O
+    mlp = rng.uniform(-0.1, 0.1, n_mlp).astype(np.float32)
+    w_all = np.concatenate([table, mlp])
+    m = np.zeros_like(w_all)
+    v = np.zeros_like(w_all)
+    n = 2048
+    batches = [make_batch_np(w, n, 11 + i) for i in range(4)]
+    step = [0]
+
+    def ref_step(pos, tgt):
+        ps, ts = ro.morton_sort(pos, tgt)
+        r = ro.train(tag, sp, w_all[:table.size], w_all[table.size:], ps, ts)
+        params = ro.adam_params(w["lr"], w["lr"], 0.9, 0.99, 1e-15, 0.0, 0.0,
+                                table.size, n_mlp, step[0])
+        slots = table.size // 2
+        bits = np.unpackbits(r["mask"].view(np.uint8), bitorder="little")[:slots]
+        idx = (np.nonzero(bits)[0] * 2).astype(np.uint32)
+        wh = w_all[:table.size]
+        ro.adam_sparse(wh, r["grad_hash"], m[:table.size], v[:table.size],
+                       params, idx)
+        ro.adam_dense(w_all[table.size:], r["grad_mlp"], m[table.size:],
+                      v[table.size:], params)
+        step[0] += 1
+        return float(r["loss_partials"].sum()) / n
+
+    for i in range(args.warmup):
+        ref_step(*batches[i % 4])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        ref_step(*batches[i % 4])
+    el = time.perf_counter() - t0
+    sps = args.steps * n / el
+    val = sps / w["batch"]
+    unit = "steps/s (2^18-point batches)"
+    return {"impl": "reference",
+            "metric": "training steps/s (HashGrid+FusedMLP, 2^18-point batches)",
+            "value": val, "unit": unit, "n_gpus": 0, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w["desc"],
+                       "sample_points_per_step": n},
+            "cpu_baseline": {"value": val, "unit": unit,
+                             "cores": os.cpu_count(), "kind": "reference",
+                             "sample": f"{args.steps} steps of {n} points through "
+                                       "the reference's generated train kernel "
+                                       "(MSL run as C++, one std::thread per "
+                                       "Metal thread), its Morton sort and its "
+                                       "sparse/dense Adam kernels"},
+            "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="sdf3d", choices=sorted(WORKLOADS))
+    ap.add_argument("--family", default="Auto")
+    ap.add_argument("--grad", default="F32")
+    ap.add_argument("--no-morton", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = WORKLOADS[args.workload]
+    rank, world, local = dist_setup(args)
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, w)), flush=True)
+        return
+
+    import torch
+    import tmnn_b200 as t
+    torch.cuda.set_device(local)
+    tr = t.Trainer.from_config(make_config(w, args.family, args.grad,
+                                           not args.no_morton),
+                               n_input=w["d"], n_output=w["O"], device=local)
+    if world > 1:
+        import torch.distributed as dist
+        uid = [t.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tr.dp_init(uid[0], rank, world)
+    plan = tr.plan()
+    B = w["batch"]
+    # device-resident pool of distinct batches (inputs + working set > L2)
+    pool = []
+    for i in range(4):
+        p, g = make_batch_np(w, B, 1000 * rank + i)
+        pool.append((torch.from_numpy(p).cuda(), torch.from_numpy(g).cuda()))
+    stream = torch.cuda.ExternalStream(tr.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    for i in range(args.warmup):
+        tr.training_step(*pool[i % 4])
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    l0 = tr.launch_count()
+    fb, ad, ar, so, losses = [], [], [], [], []
+    ev0.record(stream)
+    for i in range(args.steps):
+        losses.append(tr.training_step(*pool[i % 4], profile=True))
+        r = tr.last_result
+        fb.append(r.fwd_bwd_ms)
+        ad.append(r.adam_ms)
+        ar.append(r.allreduce_ms)
+        so.append(r.sort_ms)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = tr.launch_count() - l0
+    ck = clocks.stop()
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    value = world * args.steps * B / (ms / 1000.0) / B
+    unit = "steps/s (2^18-point batches)"
+
+    # inference samples/s (2^20 points per call, device resident)
+    q = torch.rand((1 << 20, w["d"]), device="cuda") * 2 - 1
+    out = torch.empty((1 << 20, w["O"]), device="cuda")
+    for _ in range(3):
+        tr.inference(q, out=out)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    n_inf = 20
+    for _ in range(n_inf):
+        tr.inference(q, out=out)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    inf_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    inf_sps = world * n_inf * (1 << 20) / (inf_ms / 1000.0)
+
+    # end to end: pinned host inputs through the public API
+    e2e = None
+    if not args.no_e2e:
+        hpool = []
+        for p, g in pool:
+            hp = torch.empty(p.shape, dtype=torch.float32, pin_memory=True)
+            hg = torch.empty(g.shape, dtype=torch.float32, pin_memory=True)
+            hp.copy_(p)
+            hg.copy_(g)
+            hpool.append((hp.numpy(), hg.numpy()))
+        for i in range(3):
+            tr.training_step(*hpool[i % 4])
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            tr.training_step(*hpool[i % 4])
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+        e2e = {"value": world * args.steps / (e_ms / 1000.0), "unit": unit,
+               "h2d_bytes_per_step": int(hpool[0][0].nbytes + hpool[0][1].nbytes),
+               "d2h_bytes_per_step": 8}
+
+    if rank != 0:
+        tr.close()
+        return
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs")
+    peak_note = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    nc = 1 << w["d"]
+    tbytes = 2 if w["table"] == "F16" else 4
+    per_sample = w["L"] * nc * w["F"] * (tbytes + 4) + (w["d"] + w["O"]) * 4
+    fb_ms = statistics.mean(fb)
+    achieved = per_sample * B / (fb_ms / 1000.0) / 1e9
+    traffic = NCU_TRAFFIC_PER_SAMPLE.get((args.workload, plan["family"]))
+    n_params = tr.hash_count + tr.mlp_count
+    adam_bytes = n_params * (4 * 7 + (2 if w["table"] == "F16" else 0)) + \
+        (n_params // 2)  # w,m,v r/w + grad r/w + touched
+    line = {
+        "metric": "training steps/s (HashGrid+FusedMLP, 2^18-point batches)",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 table / f32 accumulate" if w["table"] == "F16" else "f32",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "desc": w["desc"],
+                   "batch_per_gpu": B, "global_batch": B * world,
+                   "parallelism": f"dp{world}", "family": plan["family"],
+                   "hash_grad_format": args.grad,
+                   "morton_sort": not args.no_morton,
+                   "l2": "no flush: per-step working set (fp32 params, m, v, "
+                         "grads, fp16 gather copy) exceeds the 126 MB L2"},
+        "samples_per_s": value * B,
+        "inference_samples_per_s": inf_sps,
+        "final_loss": losses[-1],
+        "phase_ms": {"sort": statistics.mean(so), "fwd_bwd": fb_ms,
+                     "allreduce": statistics.mean(ar),
+                     "adam": statistics.mean(ad)},
+        "roofline": {"kernel": "fwd_bwd (" + plan["family"] + ")",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": peak_note,
+                     "algorithmic_bytes_per_sample": per_sample,
+                     "traffic": None if traffic is None else traffic * B},
+        "roofline_adam": {"bound": "hbm",
+                          "achieved": adam_bytes / (statistics.mean(ad) / 1e3) / 1e9,
+                          "peak": hbm, "unit": "GB/s",
+                          "frac": adam_bytes / (statistics.mean(ad) / 1e3) / 1e9 / hbm},
+        "gpu_launches": int(launches),
+        "clocks": ck,
+        "e2e": e2e,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(w)
+    tr.close()
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,279 @@
+/*
+ * tmnn_cuda.h -- C ABI of the B200 (sm_100a) implementation of
+ * tiny-metal-nn's neural-field hot path: multiresolution HashGrid encoding,
+ * FullyFusedMLP forward/backward and fused Adam, with the training-step
+ * lifecycle around them.
+ *
+ * This ABI replaces tmnn's Metal device seam and runtime root:
+ *   - src/tiny_metal_nn/runtime/metal_device.h:60-164 (probe, buffers,
+ *     command buffers, compile_pipeline, encode_dispatch, blit fill/copy),
+ *   - include/tiny-metal-nn/metal_context.h:105-149 (MetalContext) with its
+ *     pipeline registry / prewarm and command-batch pool,
+ * and is what tmnn's ITrainerRuntime implementation
+ * (include/tiny-metal-nn/trainer.h:136-219, DefaultRuntime in
+ * src/tiny_metal_nn/runtime/default_trainer.cpp:836-2414) calls instead.
+ * Each entry point below cites the reference interface it replaces.
+ *
+ * Conventions
+ *   - Every function returns tmnn_status (0 = OK) and never throws.  The
+ *     message of the last failure on the calling thread is returned by
+ *     tmnn_cuda_last_error().
+ *   - Host arrays are float32, row-major: positions [N x spatial_dims],
+ *     targets / outputs / d_output [N x num_outputs].  With TMNN_PTR_DEVICE
+ *     in `flags` the same arguments are CUDA device pointers (zero copy).
+ *   - One context = one GPU = one CUDA stream.  Calls on one context are
+ *     serialised by the caller; a concurrent call fails with
+ *     TMNN_ERR_CONCURRENT_CALL (the reference's in-flight guard,
+ *     src/python/tmnn_pybind.cpp training_step).
+ */
+#ifndef TMNN_CUDA_H
+#define TMNN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMNN_CUDA_ABI_VERSION 1
+
+/* Status codes mirror tmnn::DiagnosticCode
+ * (include/tiny-metal-nn/diagnostics.h:36-54). */
+typedef enum tmnn_status {
+  TMNN_OK = 0,
+  TMNN_ERR_INVALID_ARGUMENT = 1,
+  TMNN_ERR_NULL_OBJECT = 2,
+  TMNN_ERR_GPU_UNAVAILABLE = 8,
+  TMNN_ERR_KERNEL_UNAVAILABLE = 10,
+  TMNN_ERR_UNSUPPORTED_OPERATION = 11,
+  TMNN_ERR_CONFIGURATION_CONFLICT = 14,
+  TMNN_ERR_SCHEMA_MISMATCH = 15,
+  TMNN_ERR_OPERATION_FAILED = 16,
+  TMNN_ERR_CONCURRENT_CALL = 17,
+  TMNN_ERR_CAPACITY = 18
+} tmnn_status;
+
+typedef enum tmnn_loss { TMNN_LOSS_L2 = 0, TMNN_LOSS_L1 = 1,
+                         TMNN_LOSS_HUBER = 2, TMNN_LOSS_COSINE = 3 } tmnn_loss;
+
+/* Network families: tmnn::NetworkFamily
+ * (include/tiny-metal-nn/detail/network_planning.h:29-33). */
+typedef enum tmnn_family {
+  TMNN_FAMILY_AUTO = -1,
+  TMNN_FAMILY_FULLY_FUSED = 0, /* one persistent tcgen05 kernel per step */
+  TMNN_FAMILY_TILED = 1,       /* encode / MLP / scatter as separate kernels */
+  TMNN_FAMILY_SAFE_DEBUG = 2   /* fp32 CUDA-core kernels, reference order,
+                                  bounds-checked table indices */
+} tmnn_family;
+
+/* Hash-table gradient format.  FIXED16 is the reference's int32 fixed point
+ * (int(d*w*65536), truncation; mlp_kernel_emitter.cpp:20, :735-738).  F32 is
+ * a float accumulator for batches where 2^-16 quantisation underflows. */
+typedef enum tmnn_grad_format { TMNN_GRAD_FIXED16 = 0, TMNN_GRAD_F32 = 1 }
+    tmnn_grad_format;
+
+typedef enum tmnn_dtype { TMNN_DTYPE_F32 = 0, TMNN_DTYPE_F16 = 1 } tmnn_dtype;
+
+/* KernelSpec fields the hot path needs (include/tiny-metal-nn/kernels/
+ * kernel_spec.h:17-58), validated with kernel_spec.cpp:12-44's limits. */
+typedef struct tmnn_spec {
+  int32_t n_levels;             /* L, [1, 32] */
+  int32_t n_features_per_level; /* F, {1, 2, 4} */
+  int32_t log2_hashmap_size;    /* [10, 24] */
+  int32_t spatial_dims;         /* 3 or 4 */
+  float base_resolution;
+  float per_level_scale;
+  int32_t hidden_dim;           /* (0, 512] */
+  int32_t num_hidden_layers;    /* [1, 8] */
+  int32_t num_outputs;          /* >= 1 */
+  int32_t loss;                 /* tmnn_loss */
+  float huber_delta;
+  int32_t table_dtype;          /* tmnn_dtype of the gather copy of the
+                                   table; master weights are always fp32 */
+} tmnn_spec;
+
+/* TrainerConfig + WeightInitConfig (include/tiny-metal-nn/trainer.h:34-61,
+ * include/tiny-metal-nn/weight_init.h:113-141) plus this build's knobs. */
+typedef struct tmnn_train_cfg {
+  int32_t batch_size;
+  float lr_encoding, lr_network, beta1, beta2, epsilon, l1_reg, l2_reg;
+  float grad_clip, weight_decay;
+  /* weight init */
+  int32_t hash_init;            /* 0 Uniform, 1 Zero */
+  float hash_init_range;
+  int32_t mlp_init;             /* 0 KaimingUniform 1 KaimingNormal
+                                   2 XavierUniform 3 XavierNormal 4 Uniform
+                                   5 Normal 6 Zero */
+  int32_t mlp_nonlinearity;     /* 0 Linear 1 ReLU 2 LeakyReLU 3 Tanh 4 Sigmoid */
+  float mlp_uniform_range, mlp_normal_stddev, mlp_kaiming_a;
+  uint64_t seed;
+  /* execution */
+  int32_t family;               /* tmnn_family */
+  int32_t hash_grad_format;     /* tmnn_grad_format */
+  int32_t morton_sort;          /* 1: Morton-sort every training batch */
+  int32_t sparse_hash_adam;     /* -1 auto (sparse iff l1_reg == 0), 0, 1 */
+  int32_t active_levels;        /* <= 0: all levels receive gradients */
+  int32_t reserved[7];
+} tmnn_train_cfg;
+
+/* TrainingStepResult (include/tiny-metal-nn/common.h:97-110), reduced. */
+typedef struct tmnn_step_result {
+  float loss;          /* mean loss over the (global) batch */
+  uint32_t step;       /* logical step that completed */
+  uint32_t batch_size; /* points processed by this rank */
+  int32_t numerics_ok; /* 1 when loss and update were finite */
+  float gpu_ms;        /* device time of the step (TMNN_PROFILE) */
+  int32_t family;      /* family that ran */
+  float sort_ms;       /* device time of upload + Morton sort (TMNN_PROFILE) */
+  float fwd_bwd_ms;    /* device time of forward/backward/scatter */
+  float allreduce_ms;  /* device time of the gradient allreduce */
+  float adam_ms;       /* device time of Adam + gradient reset */
+} tmnn_step_result;
+
+/* RuntimeBufferRole (include/tiny-metal-nn/detail/runtime_authority.h:68-79) */
+typedef enum tmnn_buffer_role {
+  TMNN_BUF_HASH_WEIGHTS = 1,
+  TMNN_BUF_MLP_WEIGHTS = 2,
+  TMNN_BUF_GRAD_HASH = 3,
+  TMNN_BUF_GRAD_MLP = 4,
+  TMNN_BUF_FUSED_WEIGHTS = 7,
+  TMNN_BUF_FUSED_M = 8,
+  TMNN_BUF_FUSED_V = 9,
+  TMNN_BUF_HASH_GATHER = 20, /* fp16 gather copy (table_dtype == F16) */
+  TMNN_BUF_TOUCHED = 21      /* u8 per tracked slot (pair when F == 2) */
+} tmnn_buffer_role;
+
+typedef struct tmnn_buffer_view {
+  void *device_ptr;
+  size_t bytes;
+  int32_t dtype; /* 0 f32, 1 f16, 2 i32, 3 u8 */
+} tmnn_buffer_view;
+
+/* NetworkPlan (include/tiny-metal-nn/detail/network_planning.h:120-174). */
+typedef struct tmnn_plan {
+  int32_t family;          /* selected tmnn_family */
+  int32_t fallback_reason; /* tmnn::PlannerFallbackReason value */
+  uint32_t mlp_weight_count;
+  uint64_t hash_grid_size;
+  uint64_t device_bytes;   /* resident device memory of the context */
+  int32_t n_levels, n_features_per_level, spatial_dims, num_outputs;
+  char reason[128];
+} tmnn_plan;
+
+#define TMNN_PTR_DEVICE 1u  /* array arguments are device pointers */
+#define TMNN_PROFILE 2u     /* time the step with CUDA events */
+
+typedef struct tmnn_ctx tmnn_ctx;
+
+/* Defaults of TrainerConfig / WeightInitConfig. */
+void tmnn_cuda_default_train_cfg(tmnn_train_cfg *cfg);
+/* KernelSpec::validate (kernel_spec.cpp:12-44).  Message via last_error. */
+tmnn_status tmnn_cuda_validate_spec(const tmnn_spec *spec);
+
+/* MetalContext::create + DefaultRuntime ctor (default_trainer.cpp:836-869):
+ * allocates the parameter store, runs the Philox weight init, zeroes Adam. */
+tmnn_status tmnn_cuda_ctx_create(int device, const tmnn_spec *spec,
+                                 const tmnn_train_cfg *cfg, tmnn_ctx **out);
+/* try_create_from_config (include/tiny-metal-nn/factory_json.h:284-361):
+ * tcnn-style JSON {encoding, network, loss, optimizer, weight_init,
+ * batch_size}; plus an optional "b200" object for this build's knobs. */
+tmnn_status tmnn_cuda_ctx_create_from_json(int device, uint32_t n_input,
+                                           uint32_t n_output, const char *json,
+                                           tmnn_ctx **out);
+/* ~DefaultRuntime (drains the stream, releases device memory). */
+tmnn_status tmnn_cuda_ctx_destroy(tmnn_ctx *ctx);
+
+/* ITrainerRuntime::set_initial_weights (trainer.h:186-196): also resets the
+ * optimizer state and the step counter.  NULL/0 skips a buffer. */
+tmnn_status tmnn_cuda_set_initial_weights(tmnn_ctx *ctx, const float *hash,
+                                          size_t hash_count, const float *mlp,
+                                          size_t mlp_count);
+/* Host copy of the live weights (RuntimeAuthority buffer read-back). */
+tmnn_status tmnn_cuda_get_weights(tmnn_ctx *ctx, float *hash, size_t hash_count,
+                                  float *mlp, size_t mlp_count);
+
+/* ITrainerRuntime::training_step (trainer.h:140-141,
+ * default_trainer.cpp:883-1045): Morton sort, fused forward/backward/scatter,
+ * [data-parallel gradient allreduce], Adam, gradient reset. */
+tmnn_status tmnn_cuda_train_step(tmnn_ctx *ctx, const float *positions,
+                                 const float *targets, uint32_t n,
+                                 uint32_t flags, tmnn_step_result *result);
+
+/* The forward/backward half of training_step without the optimizer: Morton
+ * sort, fused forward/backward/scatter with the internal loss, gradients
+ * ACCUMULATED into the gradient buffers (the command batch that
+ * submit_forward_backward_batch encodes, training_step_execution.cpp:458-508).
+ * *loss_sum receives the summed (not averaged) loss of this batch. */
+tmnn_status tmnn_cuda_forward_backward(tmnn_ctx *ctx, const float *positions,
+                                       const float *targets, uint32_t n,
+                                       uint32_t flags, double *loss_sum);
+
+/* ITrainerRuntime::forward_for_training (trainer.h:145-149): outputs for an
+ * external loss, in input order. */
+tmnn_status tmnn_cuda_forward(tmnn_ctx *ctx, const float *positions,
+                              float *outputs, uint32_t n, uint32_t flags);
+/* ITrainerRuntime::zero_gradients / backward_accumulate / adam_step
+ * (trainer.h:160-177; default_trainer.cpp:1300-1443). */
+tmnn_status tmnn_cuda_zero_grads(tmnn_ctx *ctx);
+tmnn_status tmnn_cuda_backward_accumulate(tmnn_ctx *ctx,
+                                          const float *positions,
+                                          const float *d_output, uint32_t n,
+                                          uint32_t flags);
+tmnn_status tmnn_cuda_adam_step(tmnn_ctx *ctx);
+
+/* Trainer::evaluate -> DefaultEvaluator::evaluate
+ * (default_trainer.cpp:321-465). */
+tmnn_status tmnn_cuda_evaluate(tmnn_ctx *ctx, const float *positions,
+                               float *outputs, uint32_t n, uint32_t flags);
+
+/* Encoding only (parity instrument): features [n x L*F] f32, and when
+ * non-NULL the first table index of every corner [n x L x 2^d] (u32) and the
+ * base grid cell [n x L x d] (i32). Host pointers. */
+tmnn_status tmnn_cuda_debug_encode(tmnn_ctx *ctx, const float *positions,
+                                   uint32_t n, float *features,
+                                   uint32_t *corner_index, int32_t *cells);
+
+/* OptimizerStateBlob v1 (default_trainer.cpp:83-100, :1645-1768;
+ * docs/CHECKPOINT-CONTRACT.md:31-82): 4 sections [m_hash, v_hash, m_mlp,
+ * v_mlp], each a little-endian u32 byte length then raw fp32 bytes. With
+ * buf == NULL the required length is returned in *len. */
+tmnn_status tmnn_cuda_export_opt_state(tmnn_ctx *ctx, uint8_t *buf, size_t cap,
+                                       size_t *len, uint32_t *step);
+tmnn_status tmnn_cuda_import_opt_state(tmnn_ctx *ctx, const uint8_t *buf,
+                                       size_t len, uint32_t step);
+/* ITrainerRuntime::reset_optimizer: zero m/v, step = 0. */
+tmnn_status tmnn_cuda_reset_optimizer(tmnn_ctx *ctx);
+tmnn_status tmnn_cuda_get_step(tmnn_ctx *ctx, uint32_t *step);
+
+/* RuntimeAuthority::buffer (runtime_authority.h:110-121). */
+tmnn_status tmnn_cuda_get_buffer(tmnn_ctx *ctx, int32_t role,
+                                 tmnn_buffer_view *view);
+/* Host copy of a whole buffer (RuntimeBufferView::cpu_data read-back);
+ * bytes must equal the buffer's size. */
+tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *ctx, int32_t role, void *host,
+                                  size_t bytes);
+/* NetworkPlan of the context (network_planner.cpp:132-290). */
+tmnn_status tmnn_cuda_get_plan(tmnn_ctx *ctx, tmnn_plan *plan);
+/* The context's CUDA stream (cudaStream_t) for interop. */
+tmnn_status tmnn_cuda_get_stream(tmnn_ctx *ctx, void **stream);
+tmnn_status tmnn_cuda_synchronize(tmnn_ctx *ctx);
+
+/* Data parallelism (no reference counterpart: tmnn is single-device).
+ * unique_id: 128 bytes of an ncclUniqueId made by rank 0
+ * (tmnn_cuda_dp_unique_id) and broadcast by the caller.  After this call
+ * every train_step / adam_step sums gradients over the ranks with one NCCL
+ * allreduce (and ORs the touched-slot map), and divides by the global batch. */
+tmnn_status tmnn_cuda_dp_unique_id(uint8_t out[128]);
+tmnn_status tmnn_cuda_dp_init(tmnn_ctx *ctx, const uint8_t unique_id[128],
+                              int rank, int world);
+
+/* Message of the last failure on this thread ("" if none). */
+const char *tmnn_cuda_last_error(void);
+/* Kernels launched by this context since creation (instrumentation). */
+tmnn_status tmnn_cuda_launch_count(tmnn_ctx *ctx, uint64_t *count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -39,6 +39,10 @@ SPECS = {
     "f4": (4, 4, 10, 3, 16, 2, 1, 0, 4.0, 2.0, 1.0),
     "h3": (2, 2, 10, 3, 8, 3, 1, 0, 4.0, 2.0, 1.0),
     "cos": (4, 2, 10, 3, 16, 1, 3, 3, 4.0, 1.5, 1.0),
+    # bench.py reference arm workloads
+    "bench_sdf3d": (16, 2, 19, 3, 64, 1, 1, 1, 16.0, 1.447, 1.0),
+    "bench_image": (16, 2, 15, 3, 64, 2, 3, 0, 16.0, 1.5, 1.0),
+    "bench_field4d": (16, 2, 22, 4, 64, 2, 4, 0, 8.0, 1.5, 1.0),
 }
 
 

@@ -1,0 +1,85 @@
+"""CPU-side checks of the C ABI: the library loads, exports every entry point
+include/tmnn_cuda.h declares, and validates configurations (the JSON front
+end runs before any device work, so its errors surface without a GPU)."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "tmnn_cuda.h")
+LIB = os.path.join(ROOT, "tiny-metal-nn_b200", "libtmnn_cuda.so")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(tmnn_cuda_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    out = subprocess.run(["nm", "-D", "--defined-only", LIB], check=True,
+                         capture_output=True, text=True).stdout
+    exported = set(re.findall(r" T (tmnn_cuda_\w+)", out))
+    missing = [s for s in declared_symbols() if s not in exported]
+    assert not missing, missing
+
+
+def test_python_binding_covers_header():
+    import tmnn_b200._abi as abi
+    assert sorted(abi.SYMBOLS) == declared_symbols()
+
+
+def test_library_is_sm100a_only():
+    out = subprocess.run(["/usr/local/cuda/bin/cuobjdump", "--list-elf", LIB],
+                         capture_output=True, text=True).stdout
+    assert "sm_100a" in out
+
+
+def test_default_config_matches_reference_defaults():
+    import tmnn_b200 as t
+    from tmnn_b200 import _abi
+    c = _abi.TrainCfg()
+    t.lib.tmnn_cuda_default_train_cfg(C.byref(c))
+    # TrainerConfig (trainer.h:34-61) and WeightInitConfig (weight_init.h)
+    assert c.batch_size == 1024
+    assert abs(c.lr_encoding - 1e-2) < 1e-9 and abs(c.lr_network - 1e-3) < 1e-9
+    assert abs(c.beta1 - 0.9) < 1e-7 and abs(c.beta2 - 0.99) < 1e-7
+    assert c.seed == 42 and abs(c.hash_init_range - 1e-4) < 1e-10
+
+
+def _create(cfg_json, n_in=3, n_out=1):
+    import tmnn_b200 as t
+    h = C.c_void_p()
+    st = t.lib.tmnn_cuda_ctx_create_from_json(0, n_in, n_out, cfg_json.encode(),
+                                              C.byref(h))
+    return st, t._abi.last_error(), h
+
+
+@pytest.mark.parametrize("cfg,frag", [
+    ('{"encoding": {"n_levels": 0}}', "encoding.n_levels: must be positive"),
+    ('{"encoding": {"otype": "Frequency"}}', "unsupported encoding otype"),
+    ('{"encoding": {"interpolation": "Nearest"}}', "only 'Linear'"),
+    ('{"network": {"activation": "Tanh"}}', "only 'ReLU'"),
+    ('{"network": {"otype": "TiledMLP"}}', "reserved for later"),
+    ('{"loss": {"otype": "Huber", "huber_delta": -1}}', "loss.huber_delta"),
+    ('{"optimizer": {"learning_rate": 0}}', "optimizer.learning_rate"),
+    ('{"weight_init": {"mlp_init": "Orthogonal"}}', "allowed: KaimingUniform"),
+    ('{"bogus": 1}', "config.bogus: unknown key"),
+    ('{"encoding": {"n_levels": 2.5}}', "must be an integer"),
+    ('{"encoding": ', "json:"),
+])
+def test_config_errors_reported_without_gpu(cfg, frag):
+    st, msg, _ = _create(cfg)
+    assert st == 1, (st, msg)
+    assert frag in msg, msg
+
+
+def test_valid_config_fails_cleanly_without_gpu():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    st, msg, h = _create('{"loss": {"otype": "L1"}, "optimizer": {"learning_rate": 0.01}}')
+    assert st != 0 and "device" in msg.lower()
+    assert not h.value

@@ -1,0 +1,39 @@
+// fused.h -- the FullyFused family: one persistent sm_100a kernel per step
+// that encodes, runs the MLP forward and backward on tcgen05 tensor cores,
+// evaluates the loss and scatters the hash-table gradients.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tmnn_cuda.h"
+#include "common.cuh"
+
+namespace tmnn {
+
+// Device-side packed weights (fp16, tensor-core layouts), rebuilt lazily
+// after every weight change.
+struct FusedWorkspace {
+  void *wpack = nullptr;
+  size_t wpack_bytes = 0;
+  bool dirty = true;
+  int ctas_per_sm = 0;
+};
+
+bool fused_supported(const tmnn_spec &spec, const tmnn_train_cfg &cfg,
+                     std::string *why);
+void fused_weights_changed(FusedWorkspace &ws);
+void fused_release(FusedWorkspace &ws);
+// Each returns the number of kernels it launched.
+int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+                const float *params, const __half *table_h, const float *pos,
+                const float *tgt, const float *dext, float inv_N, float *gm,
+                int32_t *gh_fixed, float *gh_float, uint8_t *touched,
+                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st);
+int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+                  const float *params, const __half *table_h, const float *pos,
+                  float *out, uint32_t N, int num_sms, cudaStream_t st);
+
+}  // namespace tmnn

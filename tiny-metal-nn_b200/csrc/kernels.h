@@ -1,0 +1,47 @@
+// kernels.h -- host-side launchers of the hot-path kernels.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace tmnn {
+
+// ---- reference-order fp32 kernels (kernels_exact.cu) ----
+size_t exact_scratch_floats(const NetDims &nd, int num_sms);
+void launch_train_exact(const NetDims &nd, const float *table,
+                        const float *mlp, const float *pos, const float *tgt,
+                        const float *dext, float inv_N, float *grad_mlp,
+                        int32_t *gh_fixed, float *gh_float, uint8_t *touched,
+                        double *loss_acc, uint32_t N, float *scratch,
+                        int num_sms, cudaStream_t st);
+void launch_forward_exact(const NetDims &nd, const float *table,
+                          const float *mlp, const float *pos, float *out,
+                          uint32_t N, float *scratch, int num_sms,
+                          cudaStream_t st);
+void launch_encode_debug(const NetDims &nd, const float *table,
+                         const float *pos, float *feat, uint32_t *corner_idx,
+                         int32_t *cells, uint32_t N, cudaStream_t st);
+void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
+                 int32_t *gh_fixed, float *gh_float, float *gm,
+                 uint8_t *touched, __half *table_h, int num_sms,
+                 cudaStream_t st);
+void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,
+                    cudaStream_t st);
+void launch_init_uniform(float *out, uint64_t count, float low, float high,
+                         uint64_t seed, uint32_t counter_base, cudaStream_t st);
+void launch_init_normal(float *out, uint64_t count, float mean, float stddev,
+                        uint64_t seed, uint32_t counter_base, cudaStream_t st);
+size_t morton_temp_bytes(uint32_t N);
+void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
+                         uint32_t *codes_alt, uint32_t *idx,
+                         uint32_t *perm_out, void *temp, size_t temp_bytes,
+                         cudaStream_t st);
+void launch_gather_rows(const float *src, int width, const uint32_t *perm,
+                        float *dst, uint32_t N, cudaStream_t st);
+void launch_scatter_rows(const float *src, int width, const uint32_t *perm,
+                         float *dst, uint32_t N, cudaStream_t st);
+
+}  // namespace tmnn

@@ -1,0 +1,705 @@
+// kernels_exact.cu -- fp32 CUDA-core kernels that evaluate tmnn's hot path in
+// the reference's operation order.  Compiled with --fmad=false: every
+// multiply and add is rounded separately, exactly as the CPU restatement of
+// the reference, so encodings, fixed-point hash gradients and Adam updates
+// agree bit for bit.  These kernels are the SafeDebug family, the inference
+// path's reference-order variant, and the weight initialiser / optimizer of
+// every family.
+#include <cub/device/device_radix_sort.cuh>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tmnn {
+
+// ------------------------------------------------------------ corners
+
+struct Corners {
+  uint32_t off[16];  // element offset of feature 0 of the corner's entry
+  float w[16];       // (wx*wy)*wz[*wt]
+  float wc[16][4];   // per-axis weights (scalar scatter product order)
+  int32_t bc[4];
+};
+
+// One level's 2^d corners: cell = floor(p*res), frac = p*res - cell; corners
+// enumerated dz, dy, dx (dx fastest) with dw outermost in 4D
+// (mlp_kernel_emitter.cpp:224-255, :265-268, :305-308).
+__device__ inline void level_corners(const NetDims &nd, const float *p, int l,
+                                     Corners &c) {
+  const float res = nd.res[l];
+  float frac[4];
+  for (int a = 0; a < nd.d; ++a) {
+    const float s = p[a] * res;
+    const float fl = floorf(s);
+    c.bc[a] = (int32_t)fl;
+    frac[a] = s - fl;
+  }
+  const uint64_t base = (uint64_t)l * nd.T * (uint64_t)nd.F;
+  const uint32_t mask = nd.T - 1u;
+  const int nw = nd.d == 4 ? 2 : 1;
+  int k = 0;
+  for (int dw = 0; dw < nw; ++dw)
+    for (int dz = 0; dz < 2; ++dz)
+      for (int dy = 0; dy < 2; ++dy)
+        for (int dx = 0; dx < 2; ++dx) {
+          const uint32_t h =
+              nd.d == 4 ? hash4(c.bc[0] + dx, c.bc[1] + dy, c.bc[2] + dz,
+                                c.bc[3] + dw, mask)
+                        : hash3(c.bc[0] + dx, c.bc[1] + dy, c.bc[2] + dz, mask);
+          c.off[k] = (uint32_t)(base + (uint64_t)h * nd.F);
+          const float wx = dx == 0 ? 1.0f - frac[0] : frac[0];
+          const float wy = dy == 0 ? 1.0f - frac[1] : frac[1];
+          const float wz = dz == 0 ? 1.0f - frac[2] : frac[2];
+          float w = wx * wy;
+          w = w * wz;
+          c.wc[k][0] = wx;
+          c.wc[k][1] = wy;
+          c.wc[k][2] = wz;
+          if (nd.d == 4) {
+            const float wt = dw == 0 ? 1.0f - frac[3] : frac[3];
+            w = w * wt;
+            c.wc[k][3] = wt;
+          }
+          c.w[k] = w;
+          ++k;
+        }
+}
+
+__device__ inline void level_features(const NetDims &nd, const float *table,
+                                      const Corners &c, float *feat) {
+  const int nc = 1 << nd.d;
+  for (int f = 0; f < nd.F; ++f) {
+    float acc = 0.0f;
+    for (int k = 0; k < nc; ++k) acc = acc + c.w[k] * table[c.off[k] + f];
+    feat[f] = acc;
+  }
+}
+
+// ------------------------------------------------------------ forward
+
+// acts: [H][W] activations (row k = output of hidden layer k); y: [O].
+// Encode fused with W0 level by level (mlp_kernel_emitter.cpp:279-296,
+// :343-358), bias+ReLU, hidden layers (:2962-2970), output from the bias
+// (:2983-2997).
+__device__ void forward_point(const NetDims &nd, const float *table,
+                              const float *mlp, const float *p, float *acts,
+                              float *y) {
+  const int W = nd.W;
+  float *h0 = acts;
+  for (int j = 0; j < W; ++j) h0[j] = 0.0f;
+  const bool vec2 = nd.F == 2 && nd.d == 3;
+  for (int l = 0; l < nd.L; ++l) {
+    Corners c;
+    float feat[4];
+    level_corners(nd, p, l, c);
+    level_features(nd, table, c, feat);
+    if (vec2) {
+      const float *wa = mlp + nd.w_off[0] + (int64_t)(2 * l) * W;
+      const float *wb = wa + W;
+      for (int j = 0; j < W; ++j) {
+        const float t = feat[0] * wa[j] + feat[1] * wb[j];
+        h0[j] = h0[j] + t;
+      }
+    } else {
+      for (int f = 0; f < nd.F; ++f) {
+        const float *wr = mlp + nd.w_off[0] + (int64_t)(l * nd.F + f) * W;
+        for (int j = 0; j < W; ++j) h0[j] = h0[j] + feat[f] * wr[j];
+      }
+    }
+  }
+  for (int j = 0; j < W; ++j) {
+    const float t = h0[j] + mlp[nd.b_off[0] + j];
+    h0[j] = t > 0.0f ? t : 0.0f;
+  }
+  for (int k = 1; k < nd.H; ++k) {
+    const float *hin = acts + (k - 1) * W;
+    float *hout = acts + k * W;
+    const float *Wk = mlp + nd.w_off[k];
+    for (int j = 0; j < W; ++j) {
+      float acc = 0.0f;
+      for (int i = 0; i < W; ++i) acc = acc + hin[i] * Wk[(int64_t)i * W + j];
+      const float t = acc + mlp[nd.b_off[k] + j];
+      hout[j] = t > 0.0f ? t : 0.0f;
+    }
+  }
+  const float *hl = acts + (nd.H - 1) * W;
+  const float *Wo = mlp + nd.w_off[nd.H];
+  for (int m = 0; m < nd.O; ++m) {
+    float acc = mlp[nd.b_off[nd.H] + m];
+    for (int j = 0; j < W; ++j) acc = acc + hl[j] * Wo[(int64_t)j * nd.O + m];
+    y[m] = acc;
+  }
+}
+
+// Loss and dL/dy (mlp_kernel_emitter.cpp:562-670); multi-output loss is the
+// sum over outputs.
+__device__ float point_loss(const NetDims &nd, const float *y, const float *t,
+                            float inv_N, float *d) {
+  const int O = nd.O;
+  if (nd.loss == 3) {
+    float dot = 0.0f, pn = 0.0f, tn = 0.0f;
+    for (int m = 0; m < O; ++m) {
+      dot = dot + y[m] * t[m];
+      pn = pn + y[m] * y[m];
+      tn = tn + t[m] * t[m];
+    }
+    const float pred_norm = sqrtf(pn + 1e-8f);
+    const float target_norm = sqrtf(tn + 1e-8f);
+    const float denom = pred_norm * target_norm;
+    const float cosine = dot / denom;
+    const float pnd = pn + 1e-8f;
+    for (int m = 0; m < O; ++m) {
+      const float a = (cosine * y[m]) / pnd;
+      const float b = t[m] / denom;
+      d[m] = (a - b) * inv_N;
+    }
+    return 1.0f - cosine;
+  }
+  float loss = 0.0f;
+  for (int m = 0; m < O; ++m) {
+    const float r = y[m] - t[m];
+    float term;
+    if (nd.loss == 0) {
+      term = r * r;
+      d[m] = (2.0f * r) * inv_N;
+    } else if (nd.loss == 1) {
+      term = fabsf(r);
+      d[m] = (r > 0.0f ? 1.0f : (r < 0.0f ? -1.0f : 0.0f)) * inv_N;
+    } else {
+      const float ar = fabsf(r), delta = nd.huber_delta;
+      if (ar <= delta) {
+        term = (0.5f * r) * r;
+        d[m] = r * inv_N;
+      } else {
+        term = delta * (ar - 0.5f * delta);
+        d[m] = (delta * (r > 0.0f ? 1.0f : -1.0f)) * inv_N;
+      }
+    }
+    loss = loss + term;
+  }
+  return loss;
+}
+
+struct GradSink {
+  float *gm;          // MLP gradient accumulator (shared or global)
+  int32_t *gh_fixed;  // fixed-point hash gradients
+  float *gh_float;    // float hash gradients
+  uint8_t *touched;
+};
+
+__device__ inline void scatter_one(const NetDims &nd, const GradSink &g,
+                                   uint32_t off, float v) {
+  if (nd.grad_fixed)
+    atomicAdd(g.gh_fixed + off, fixed_trunc(v * kGradScale));
+  else
+    atomicAdd(g.gh_float + off, v);
+}
+
+// Backward of one point (mlp_kernel_emitter.cpp:3061-3155 with
+// emitHashScatter :672-901).  d: dL/dy [O]; acts hold the forward
+// activations and are overwritten with pre-activation gradients.
+__device__ void backward_point(const NetDims &nd, const float *table,
+                               const float *mlp, const float *p, float *acts,
+                               const float *d, const GradSink &g) {
+  const int W = nd.W, O = nd.O, H = nd.H;
+  float *hl = acts + (H - 1) * W;
+  const float *Wo = mlp + nd.w_off[H];
+  for (int j = 0; j < W; ++j) {
+    const float hv = hl[j];
+    float dpre = 0.0f;
+    for (int m = 0; m < O; ++m) {
+      atomicAdd(g.gm + nd.w_off[H] + (int64_t)j * O + m, d[m] * hv);
+      dpre = dpre + d[m] * Wo[(int64_t)j * O + m];
+    }
+    hl[j] = dpre * (hv > 0.0f ? 1.0f : 0.0f);
+  }
+  for (int m = 0; m < O; ++m) atomicAdd(g.gm + nd.b_off[H] + m, d[m]);
+  for (int k = H - 1; k >= 1; --k) {
+    const float *dk = acts + k * W;
+    float *hin = acts + (k - 1) * W;
+    const float *Wk = mlp + nd.w_off[k];
+    for (int i = 0; i < W; ++i) {
+      const float hv = hin[i];
+      for (int j = 0; j < W; ++j)
+        atomicAdd(g.gm + nd.w_off[k] + (int64_t)i * W + j, dk[j] * hv);
+      float acc = 0.0f;
+      for (int j = 0; j < W; ++j) acc = acc + dk[j] * Wk[(int64_t)i * W + j];
+      hin[i] = acc * (hv > 0.0f ? 1.0f : 0.0f);
+    }
+    for (int j = 0; j < W; ++j) atomicAdd(g.gm + nd.b_off[k] + j, dk[j]);
+  }
+  const float *h0 = acts;
+  const bool vec2 = nd.F == 2 && nd.d == 3;
+  const int nc = 1 << nd.d;
+  for (int l = 0; l < nd.active_levels; ++l) {
+    Corners c;
+    float feat[4];
+    level_corners(nd, p, l, c);
+    level_features(nd, table, c, feat);
+    if (vec2) {
+      const int64_t r0 = nd.w_off[0] + (int64_t)(2 * l) * W, r1 = r0 + W;
+      for (int j = 0; j < W; ++j) {
+        atomicAdd(g.gm + r0 + j, h0[j] * feat[0]);
+        atomicAdd(g.gm + r1 + j, h0[j] * feat[1]);
+      }
+      float dfx = 0.0f, dfy = 0.0f;
+      for (int j = 0; j < W; ++j) {
+        dfx = dfx + h0[j] * mlp[r0 + j];
+        dfy = dfy + h0[j] * mlp[r1 + j];
+      }
+      for (int k = 0; k < nc; ++k) {
+        scatter_one(nd, g, c.off[k], dfx * c.w[k]);
+        scatter_one(nd, g, c.off[k] + 1, dfy * c.w[k]);
+        g.touched[c.off[k] >> 1] = 1;
+      }
+    } else {
+      for (int f = 0; f < nd.F; ++f) {
+        const int64_t r = nd.w_off[0] + (int64_t)(l * nd.F + f) * W;
+        for (int j = 0; j < W; ++j) atomicAdd(g.gm + r + j, h0[j] * feat[f]);
+        float df = 0.0f;
+        for (int j = 0; j < W; ++j) df = df + h0[j] * mlp[r + j];
+        for (int k = 0; k < nc; ++k) {
+          float v = df * c.wc[k][0];
+          v = v * c.wc[k][1];
+          v = v * c.wc[k][2];
+          if (nd.d == 4) v = v * c.wc[k][3];
+          const uint32_t e = c.off[k] + f;
+          scatter_one(nd, g, e, v);
+          g.touched[nd.F == 2 ? e >> 1 : e] = 1;
+        }
+      }
+    }
+  }
+  for (int j = 0; j < W; ++j) atomicAdd(g.gm + nd.b_off[0] + j, h0[j]);
+}
+
+// ------------------------------------------------------------ kernels
+
+constexpr int kExactBlock = 128;
+
+template <int WMAX>
+__global__ void __launch_bounds__(kExactBlock)
+    k_train_exact(NetDims nd, const float *__restrict__ table,
+                  const float *__restrict__ mlp, const float *__restrict__ pos,
+                  const float *__restrict__ tgt, const float *__restrict__ dext,
+                  float inv_N, float *grad_mlp, int32_t *gh_fixed,
+                  float *gh_float, uint8_t *touched, double *loss_acc,
+                  uint32_t N, int use_smem_grads, float *scratch) {
+  extern __shared__ float s_grad[];
+  __shared__ double s_loss[kExactBlock / 32];
+  if (use_smem_grads) {
+    for (uint32_t i = threadIdx.x; i < nd.mlp_count; i += blockDim.x)
+      s_grad[i] = 0.0f;
+    __syncthreads();
+  }
+  GradSink g{use_smem_grads ? s_grad : grad_mlp, gh_fixed, gh_float, touched};
+  float local_acts[WMAX > 0 ? kMaxHidden * WMAX : 1];
+  float *acts = WMAX > 0 ? local_acts
+                         : scratch + (size_t)(blockIdx.x * blockDim.x +
+                                              threadIdx.x) * nd.H * nd.W;
+  float loss = 0.0f;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < N;
+       i += gridDim.x * blockDim.x) {
+    const float *p = pos + (size_t)i * nd.d;
+    float y[64], d[64];
+    forward_point(nd, table, mlp, p, acts, y);
+    if (dext) {
+      for (int m = 0; m < nd.O; ++m) d[m] = dext[(size_t)i * nd.O + m];
+    } else {
+      loss = loss + point_loss(nd, y, tgt + (size_t)i * nd.O, inv_N, d);
+    }
+    backward_point(nd, table, mlp, p, acts, d, g);
+  }
+  // block loss reduction in double, one atomic per block
+  double lv = loss;
+  for (int o = 16; o > 0; o >>= 1) lv += __shfl_down_sync(0xffffffffu, lv, o);
+  if ((threadIdx.x & 31) == 0) s_loss[threadIdx.x >> 5] = lv;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kExactBlock / 32; ++w) t += s_loss[w];
+    if (!dext) atomicAdd(loss_acc, t);
+  }
+  if (use_smem_grads) {
+    for (uint32_t i = threadIdx.x; i < nd.mlp_count; i += blockDim.x) {
+      const float v = s_grad[i];
+      if (v != 0.0f) atomicAdd(grad_mlp + i, v);
+    }
+  }
+}
+
+template <int WMAX>
+__global__ void __launch_bounds__(kExactBlock)
+    k_forward_exact(NetDims nd, const float *__restrict__ table,
+                    const float *__restrict__ mlp, const float *__restrict__ pos,
+                    float *__restrict__ out, uint32_t N, float *scratch) {
+  float local_acts[WMAX > 0 ? kMaxHidden * WMAX : 1];
+  float *acts = WMAX > 0 ? local_acts
+                         : scratch + (size_t)(blockIdx.x * blockDim.x +
+                                              threadIdx.x) * nd.H * nd.W;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < N;
+       i += gridDim.x * blockDim.x) {
+    float y[64];
+    forward_point(nd, table, mlp, pos + (size_t)i * nd.d, acts, y);
+    for (int m = 0; m < nd.O; ++m) out[(size_t)i * nd.O + m] = y[m];
+  }
+}
+
+__global__ void k_encode_debug(NetDims nd, const float *__restrict__ table,
+                               const float *__restrict__ pos, float *feat,
+                               uint32_t *corner_idx, int32_t *cells,
+                               uint32_t N) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const int nc = 1 << nd.d;
+  for (int l = 0; l < nd.L; ++l) {
+    Corners c;
+    level_corners(nd, pos + (size_t)i * nd.d, l, c);
+    level_features(nd, table, c, feat + (size_t)i * nd.In + l * nd.F);
+    if (corner_idx)
+      for (int k = 0; k < nc; ++k)
+        corner_idx[((size_t)i * nd.L + l) * nc + k] = c.off[k];
+    if (cells)
+      for (int a = 0; a < nd.d; ++a)
+        cells[((size_t)i * nd.L + l) * nd.d + a] = c.bc[a];
+  }
+}
+
+// ------------------------------------------------------------ Adam
+
+// adam_kernel_msl.h:37-109 (unified) and :120-203 (sparse hash + dense MLP),
+// fused with the post-Adam gradient reset of the reference's step
+// (training_step_execution.cpp:1285-1294) and the refresh of the fp16
+// gather copy.  One thread per tracked hash slot (entry_width elements)
+// or per MLP weight.
+__device__ inline void adam_elem(float &w, float &m, float &v, float g,
+                                 float lr, const AdamArgs &a, float reg,
+                                 bool is_mlp) {
+  if (a.grad_clip > 0.0f)
+    g = g < -a.grad_clip ? -a.grad_clip : (g > a.grad_clip ? a.grad_clip : g);
+  if (a.weight_decay > 0.0f) {
+    const float t = (lr * a.weight_decay) * w;
+    w = w - t;
+  } else if (reg > 0.0f) {
+    if (is_mlp)
+      g = g + reg * w;
+    else
+      g = g + reg * (w > 0.0f ? 1.0f : (w < 0.0f ? -1.0f : 0.0f));
+  }
+  const float mn = a.beta1 * m + (1.0f - a.beta1) * g;
+  const float vn = a.beta2 * v + ((1.0f - a.beta2) * g) * g;
+  m = mn;
+  v = vn;
+  const float mh = mn / a.bc1;
+  const float vh = vn / a.bc2;
+  const float upd = (lr * mh) / (sqrtf(vh) + a.eps);
+  w = w - upd;
+}
+
+__global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
+                       float *__restrict__ v, int32_t *gh_fixed,
+                       float *gh_float, float *__restrict__ gm,
+                       uint8_t *__restrict__ touched, __half *table_h) {
+  const uint64_t total = a.slots + a.mlp_count;
+  for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (uint64_t)gridDim.x * blockDim.x) {
+    if (t < a.slots) {
+      const bool on = !a.sparse || touched[t];
+      if (a.sparse) touched[t] = 0;
+      for (int k = 0; k < a.entry_width; ++k) {
+        const uint64_t e = t * a.entry_width + k;
+        float g;
+        if (a.grad_fixed) {
+          g = (float)gh_fixed[e] * kInvGradScale;
+          gh_fixed[e] = 0;
+        } else {
+          g = gh_float[e];
+          gh_float[e] = 0.0f;
+        }
+        if (!on) continue;
+        float wv = w[e], mv = m[e], vv = v[e];
+        adam_elem(wv, mv, vv, g, a.lr_hash, a, a.l1_hash, false);
+        w[e] = wv;
+        m[e] = mv;
+        v[e] = vv;
+        if (table_h) table_h[e] = __float2half_rn(wv);
+      }
+    } else {
+      const uint64_t j = t - a.slots;
+      const uint64_t e = a.hash_count + j;
+      const float g = gm[j];
+      gm[j] = 0.0f;
+      float wv = w[e], mv = m[e], vv = v[e];
+      adam_elem(wv, mv, vv, g, a.lr_mlp, a, a.l2_mlp, true);
+      w[e] = wv;
+      m[e] = mv;
+      v[e] = vv;
+    }
+  }
+}
+
+__global__ void k_to_half(const float *__restrict__ src, __half *dst,
+                          uint64_t n) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    dst[i] = __float2half_rn(src[i]);
+}
+
+// ------------------------------------------------------------ Philox init
+
+// Philox-4x32-10 (Salmon et al., SC'11); the reference's init kernels
+// (metal_context.cpp:731-874) draw ctr = (counter_base + t, 0, 0, 0).
+__device__ inline void philox(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c[0], hi0 = __umulhi(0xD2511F53u, c[0]);
+    const uint32_t lo1 = 0xCD9E8D57u * c[2], hi1 = __umulhi(0xCD9E8D57u, c[2]);
+    const uint32_t n0 = hi1 ^ c[1] ^ k0, n2 = hi0 ^ c[3] ^ k1;
+    c[0] = n0;
+    c[1] = lo1;
+    c[2] = n2;
+    c[3] = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+__global__ void k_init_uniform(float *out, uint64_t count, float low,
+                               float high, uint32_t k0, uint32_t k1,
+                               uint32_t counter_base) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t * 4 >= count) return;
+  uint32_t c[4] = {counter_base + (uint32_t)t, 0u, 0u, 0u};
+  philox(c, k0, k1);
+  const float span = high - low;
+  for (int k = 0; k < 4; ++k) {
+    const uint64_t e = t * 4 + k;
+    if (e >= count) break;
+    const float u = (float)c[k] * (1.0f / 4294967296.0f);
+    out[e] = low + u * span;
+  }
+}
+
+__global__ void k_init_normal(float *out, uint64_t count, float mean,
+                              float stddev, uint32_t k0, uint32_t k1,
+                              uint32_t counter_base) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t * 4 >= count) return;
+  uint32_t c[4] = {counter_base + (uint32_t)t, 0u, 0u, 0u};
+  philox(c, k0, k1);
+  const float s = 1.0f / 4294967296.0f;
+  float u1 = fmaxf((float)c[0] * s, 1.0e-30f), u2 = (float)c[1] * s;
+  float u3 = fmaxf((float)c[2] * s, 1.0e-30f), u4 = (float)c[3] * s;
+  const float TWO_PI = 6.28318530718f;
+  const float r1 = sqrtf(-2.0f * logf(u1)), r2 = sqrtf(-2.0f * logf(u3));
+  const float z[4] = {r1 * cosf(TWO_PI * u2), r1 * sinf(TWO_PI * u2),
+                      r2 * cosf(TWO_PI * u4), r2 * sinf(TWO_PI * u4)};
+  for (int k = 0; k < 4; ++k) {
+    const uint64_t e = t * 4 + k;
+    if (e >= count) break;
+    out[e] = mean + stddev * z[k];
+  }
+}
+
+// ------------------------------------------------------------ Morton order
+
+__device__ inline uint32_t expand3(uint32_t v) {
+  v = (v | (v << 16)) & 0x030000FFu;
+  v = (v | (v << 8)) & 0x0300F00Fu;
+  v = (v | (v << 4)) & 0x030C30C3u;
+  v = (v | (v << 2)) & 0x09249249u;
+  return v;
+}
+__device__ inline uint32_t expand4(uint32_t v) {
+  v &= 0xFFu;
+  v = (v | (v << 16)) & 0x000F000Fu;
+  v = (v | (v << 8)) & 0x00C30C03u;
+  v = (v | (v << 4)) & 0x09090909u;
+  v = (v | (v << 2)) & 0x11111111u;
+  return v;
+}
+__device__ inline uint32_t quant(float v, float cells) {
+  const float mapped = (v * 0.5f + 0.5f) * cells;
+  return (uint32_t)fminf(fmaxf(mapped, 0.0f), cells - 1.0f);
+}
+
+// morton_sort.h:14-58 codes; the permutation is sorted by CUB's stable radix
+// sort, so equal codes keep their input order.
+__global__ void k_morton_codes(const float *__restrict__ pos, int d,
+                               uint32_t *codes, uint32_t *idx, uint32_t N) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const float *p = pos + (size_t)i * d;
+  codes[i] = d == 4 ? (expand4(quant(p[3], 256.f)) << 3) |
+                          (expand4(quant(p[2], 256.f)) << 2) |
+                          (expand4(quant(p[1], 256.f)) << 1) |
+                          expand4(quant(p[0], 256.f))
+                    : (expand3(quant(p[2], 1024.f)) << 2) |
+                          (expand3(quant(p[1], 1024.f)) << 1) |
+                          expand3(quant(p[0], 1024.f));
+  idx[i] = i;
+}
+
+__global__ void k_gather_rows(const float *__restrict__ src, int width,
+                              const uint32_t *__restrict__ perm, float *dst,
+                              uint32_t N) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)N * width) return;
+  const uint64_t row = t / width, col = t % width;
+  dst[t] = src[(uint64_t)perm[row] * width + col];
+}
+
+__global__ void k_scatter_rows(const float *__restrict__ src, int width,
+                               const uint32_t *__restrict__ perm, float *dst,
+                               uint32_t N) {
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (uint64_t)N * width) return;
+  const uint64_t row = t / width, col = t % width;
+  dst[(uint64_t)perm[row] * width + col] = src[t];
+}
+
+// ------------------------------------------------------------ launchers
+
+static int wmax_for(int W) {
+  return W <= 16 ? 16 : W <= 32 ? 32 : W <= 64 ? 64 : W <= 128 ? 128 : 0;
+}
+
+int exact_grid(uint32_t N, int num_sms) {
+  const uint32_t want = (N + kExactBlock - 1) / kExactBlock;
+  const uint32_t cap = (uint32_t)num_sms * 8u;
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+size_t exact_scratch_floats(const NetDims &nd, int num_sms) {
+  return wmax_for(nd.W) ? 0
+                        : (size_t)num_sms * 8 * kExactBlock * nd.H * nd.W;
+}
+
+void launch_train_exact(const NetDims &nd, const float *table,
+                        const float *mlp, const float *pos, const float *tgt,
+                        const float *dext, float inv_N, float *grad_mlp,
+                        int32_t *gh_fixed, float *gh_float, uint8_t *touched,
+                        double *loss_acc, uint32_t N, float *scratch,
+                        int num_sms, cudaStream_t st) {
+  if (N == 0) return;
+  const int grid = exact_grid(N, num_sms);
+  const size_t smem = (size_t)nd.mlp_count * sizeof(float);
+  const int use_smem = smem <= 96 * 1024 ? 1 : 0;
+  const size_t dyn = use_smem ? smem : 0;
+#define TMNN_TRAIN_CASE(WM)                                                   \
+  {                                                                           \
+    if (dyn > 48 * 1024)                                                      \
+      cudaFuncSetAttribute(k_train_exact<WM>,                                 \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                           (int)dyn);                                         \
+    k_train_exact<WM><<<grid, kExactBlock, dyn, st>>>(                        \
+        nd, table, mlp, pos, tgt, dext, inv_N, grad_mlp, gh_fixed, gh_float,  \
+        touched, loss_acc, N, use_smem, scratch);                             \
+  }
+  switch (wmax_for(nd.W)) {
+    case 16: TMNN_TRAIN_CASE(16) break;
+    case 32: TMNN_TRAIN_CASE(32) break;
+    case 64: TMNN_TRAIN_CASE(64) break;
+    case 128: TMNN_TRAIN_CASE(128) break;
+    default: TMNN_TRAIN_CASE(0) break;
+  }
+#undef TMNN_TRAIN_CASE
+}
+
+void launch_forward_exact(const NetDims &nd, const float *table,
+                          const float *mlp, const float *pos, float *out,
+                          uint32_t N, float *scratch, int num_sms,
+                          cudaStream_t st) {
+  if (N == 0) return;
+  const int grid = exact_grid(N, num_sms);
+  switch (wmax_for(nd.W)) {
+    case 16: k_forward_exact<16><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, N, scratch); break;
+    case 32: k_forward_exact<32><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, N, scratch); break;
+    case 64: k_forward_exact<64><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, N, scratch); break;
+    case 128: k_forward_exact<128><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, N, scratch); break;
+    default: k_forward_exact<0><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, N, scratch); break;
+  }
+}
+
+void launch_encode_debug(const NetDims &nd, const float *table,
+                         const float *pos, float *feat, uint32_t *corner_idx,
+                         int32_t *cells, uint32_t N, cudaStream_t st) {
+  if (N == 0) return;
+  k_encode_debug<<<(N + 127) / 128, 128, 0, st>>>(nd, table, pos, feat,
+                                                  corner_idx, cells, N);
+}
+
+void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
+                 int32_t *gh_fixed, float *gh_float, float *gm,
+                 uint8_t *touched, __half *table_h, int num_sms,
+                 cudaStream_t st) {
+  const uint64_t total = a.slots + a.mlp_count;
+  uint64_t blocks = (total + 255) / 256;
+  const uint64_t cap = (uint64_t)num_sms * 16;
+  if (blocks > cap) blocks = cap;
+  k_adam<<<(unsigned)blocks, 256, 0, st>>>(a, w, m, v, gh_fixed, gh_float, gm,
+                                           touched, table_h);
+}
+
+void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,
+                    cudaStream_t st) {
+  if (n == 0) return;
+  k_to_half<<<num_sms * 8, 256, 0, st>>>(src, dst, n);
+}
+
+void launch_init_uniform(float *out, uint64_t count, float low, float high,
+                         uint64_t seed, uint32_t counter_base,
+                         cudaStream_t st) {
+  const uint64_t threads = (count + 3) / 4;
+  if (!threads) return;
+  k_init_uniform<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      out, count, low, high, (uint32_t)seed, (uint32_t)(seed >> 32),
+      counter_base);
+}
+
+void launch_init_normal(float *out, uint64_t count, float mean, float stddev,
+                        uint64_t seed, uint32_t counter_base,
+                        cudaStream_t st) {
+  const uint64_t threads = (count + 3) / 4;
+  if (!threads) return;
+  k_init_normal<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+      out, count, mean, stddev, (uint32_t)seed, (uint32_t)(seed >> 32),
+      counter_base);
+}
+
+size_t morton_temp_bytes(uint32_t N) {
+  size_t bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint32_t *)nullptr,
+                                  (uint32_t *)nullptr, (uint32_t *)nullptr,
+                                  (uint32_t *)nullptr, (int)N, 0, 32);
+  return bytes;
+}
+
+// Sorted permutation of the batch by Morton code; returns perm (input index
+// of the i-th sorted point) in perm_out.
+void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
+                         uint32_t *codes_alt, uint32_t *idx,
+                         uint32_t *perm_out, void *temp, size_t temp_bytes,
+                         cudaStream_t st) {
+  if (N == 0) return;
+  k_morton_codes<<<(N + 255) / 256, 256, 0, st>>>(pos, d, codes, idx, N);
+  cub::DeviceRadixSort::SortPairs(temp, temp_bytes, codes, codes_alt, idx,
+                                  perm_out, (int)N, 0, d == 4 ? 32 : 30, st);
+}
+
+void launch_gather_rows(const float *src, int width, const uint32_t *perm,
+                        float *dst, uint32_t N, cudaStream_t st) {
+  const uint64_t n = (uint64_t)N * width;
+  if (!n) return;
+  k_gather_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, width, perm,
+                                                            dst, N);
+}
+
+void launch_scatter_rows(const float *src, int width, const uint32_t *perm,
+                         float *dst, uint32_t N, cudaStream_t st) {
+  const uint64_t n = (uint64_t)N * width;
+  if (!n) return;
+  k_scatter_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, width, perm,
+                                                             dst, N);
+}
+
+}  // namespace tmnn

@@ -1,0 +1,1112 @@
+// runtime.cu -- the host runtime behind the C ABI (include/tmnn_cuda.h).
+//
+// Plays the part of tmnn's DefaultRuntime (src/tiny_metal_nn/runtime/
+// default_trainer.cpp:836-2414) and ParameterStore (parameter_store.cpp) on a
+// CUDA stream: owns the device parameter store, runs the weight init,
+// sequences one training step (Morton sort -> forward/backward/scatter ->
+// [NCCL allreduce] -> Adam with gradient reset -> loss read-back), and
+// implements the split / accumulation API, evaluation, the optimizer
+// checkpoint blob and the network plan.
+#include <nccl.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/tmnn_cuda.h"
+#include "fused.h"
+#include "kernels.h"
+#include "runtime.h"
+
+using namespace tmnn;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct CapacityError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct ConcurrentCall : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+#define CK(x)                                                              \
+  do {                                                                     \
+    cudaError_t e_ = (x);                                                  \
+    if (e_ != cudaSuccess)                                                 \
+      throw std::runtime_error(std::string(#x) + ": " +                    \
+                               cudaGetErrorString(e_));                    \
+  } while (0)
+#define NK(x)                                                              \
+  do {                                                                     \
+    ncclResult_t r_ = (x);                                                 \
+    if (r_ != ncclSuccess)                                                 \
+      throw std::runtime_error(std::string(#x) + ": " +                    \
+                               ncclGetErrorString(r_));                    \
+  } while (0)
+
+// The emitter prints BASE/SCALE/huber with std::fixed << setprecision(6)
+// (mlp_kernel_emitter.cpp:91-92) and the kernel parses them as float.
+float round6(float x) {
+  char buf[64];
+  std::snprintf(buf, sizeof buf, "%.6f", (double)x);
+  return std::strtof(buf, nullptr);
+}
+
+template <class T>
+struct DevBuf {
+  T *p = nullptr;
+  size_t n = 0;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  void alloc(size_t count) {
+    release();
+    if (count) CK(cudaMalloc(&p, count * sizeof(T)));
+    n = count;
+  }
+  void ensure(size_t count) {
+    if (count > n) alloc(count);
+  }
+  size_t bytes() const { return n * sizeof(T); }
+};
+
+}  // namespace
+
+struct tmnn_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  tmnn_spec spec{};
+  tmnn_train_cfg cfg{};
+  NetDims nd{};
+  uint64_t hash_count = 0;
+  uint32_t mlp_count = 0;
+  uint64_t slots = 0;
+  int entry_width = 1;
+  int family = TMNN_FAMILY_SAFE_DEBUG;
+  int fallback_reason = kReasonNone;
+  std::string plan_text;
+  bool sparse = true;
+  uint32_t step = 0;
+  uint64_t launches = 0;
+  std::atomic<bool> busy{false};
+  // parameter store
+  DevBuf<float> params, m, v;
+  DevBuf<__half> table_h;
+  DevBuf<int32_t> gh_fixed;
+  DevBuf<float> gh_float, gm;
+  DevBuf<uint8_t> touched;
+  DevBuf<double> loss_acc;
+  DevBuf<float> scratch;
+  // batch staging
+  DevBuf<float> pos_in, tgt_in, pos_s, tgt_s, out_buf, out_s;
+  DevBuf<uint32_t> codes, codes_alt, idx, perm;
+  DevBuf<uint8_t> sort_tmp;
+  double *h_loss = nullptr;  // pinned
+  cudaEvent_t ev[6] = {};
+  FusedWorkspace fws;
+  // data parallelism
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+
+  float *hash_w() { return params.p; }
+  float *mlp_w() { return params.p + hash_count; }
+  const float *gather_table() const { return params.p; }
+
+  ~tmnn_ctx() {
+    if (stream) cudaStreamSynchronize(stream);
+    if (comm) ncclCommDestroy(comm);
+    if (h_loss) cudaFreeHost(h_loss);
+    for (auto e : ev)
+      if (e) cudaEventDestroy(e);
+    fused_release(fws);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+namespace {
+
+struct BusyGuard {
+  tmnn_ctx *c;
+  explicit BusyGuard(tmnn_ctx *ctx) : c(ctx) {
+    bool expected = false;
+    if (!c->busy.compare_exchange_strong(expected, true))
+      throw ConcurrentCall(
+          "another call is in progress on this context; a context is "
+          "single-threaded (use one context per thread)");
+  }
+  ~BusyGuard() { c->busy.store(false); }
+};
+
+template <class F>
+tmnn_status guarded(F &&f) {
+  try {
+    g_last_error.clear();
+    f();
+    return TMNN_OK;
+  } catch (const ConcurrentCall &e) {
+    g_last_error = e.what();
+    return TMNN_ERR_CONCURRENT_CALL;
+  } catch (const CapacityError &e) {
+    g_last_error = e.what();
+    return TMNN_ERR_CAPACITY;
+  } catch (const std::invalid_argument &e) {
+    g_last_error = e.what();
+    return TMNN_ERR_INVALID_ARGUMENT;
+  } catch (const std::exception &e) {
+    g_last_error = e.what();
+    return TMNN_ERR_OPERATION_FAILED;
+  } catch (...) {
+    g_last_error = "unknown error";
+    return TMNN_ERR_OPERATION_FAILED;
+  }
+}
+
+#define REQUIRE_CTX(c) \
+  if (!(c)) {          \
+    g_last_error = "null context"; \
+    return TMNN_ERR_NULL_OBJECT;   \
+  }
+
+// KernelSpec::validate (kernel_spec.cpp:12-44) plus this build's limits.
+void validate(const tmnn_spec &s) {
+  auto bad = [](const char *m) { throw std::invalid_argument(m); };
+  if (s.hidden_dim <= 0 || s.hidden_dim > 512)
+    bad("KernelSpec: hidden_dim must be in (0, 512]");
+  if (s.num_hidden_layers < 1 || s.num_hidden_layers > 8)
+    bad("KernelSpec: num_hidden_layers must be in [1, 8]");
+  if (s.n_levels < 1 || s.n_levels > 32)
+    bad("KernelSpec: num_levels must be in [1, 32]");
+  if (s.log2_hashmap_size < 10 || s.log2_hashmap_size > 24)
+    bad("KernelSpec: log2_hashmap_size must be in [10, 24]");
+  if (s.n_features_per_level != 1 && s.n_features_per_level != 2 &&
+      s.n_features_per_level != 4)
+    bad("KernelSpec: features_per_level must be 1, 2, or 4");
+  if (s.spatial_dims != 3 && s.spatial_dims != 4)
+    bad("KernelSpec: spatial_dims must be 3 or 4");
+  if (s.loss < TMNN_LOSS_L2 || s.loss > TMNN_LOSS_COSINE)
+    bad("KernelSpec: invalid loss type");
+  if (s.loss == TMNN_LOSS_HUBER && !(s.huber_delta > 0.0f))
+    bad("KernelSpec: Huber loss requires huber_delta > 0");
+  if (s.loss == TMNN_LOSS_COSINE && s.num_outputs < 2)
+    bad("KernelSpec: Cosine loss requires num_outputs >= 2");
+  if (s.num_outputs < 1 || s.num_outputs > 64)
+    bad("KernelSpec: num_outputs must be in [1, 64]");
+  if (!(s.base_resolution > 0.0f) || !(s.per_level_scale > 0.0f))
+    bad("KernelSpec: base_resolution and per_level_scale must be positive");
+  if (s.table_dtype != TMNN_DTYPE_F32 && s.table_dtype != TMNN_DTYPE_F16)
+    bad("tmnn_spec: table_dtype must be F32 or F16");
+}
+
+NetDims make_dims(const tmnn_spec &s, const tmnn_train_cfg &c) {
+  NetDims nd{};
+  nd.L = s.n_levels;
+  nd.F = s.n_features_per_level;
+  nd.log2T = s.log2_hashmap_size;
+  nd.d = s.spatial_dims;
+  nd.W = s.hidden_dim;
+  nd.H = s.num_hidden_layers;
+  nd.O = s.num_outputs;
+  nd.In = nd.L * nd.F;
+  nd.loss = s.loss;
+  nd.huber_delta = round6(s.huber_delta);
+  nd.active_levels =
+      c.active_levels > 0 && c.active_levels < nd.L ? c.active_levels : nd.L;
+  nd.grad_fixed = c.hash_grad_format == TMNN_GRAD_FIXED16 ? 1 : 0;
+  nd.T = 1u << nd.log2T;
+  nd.hash_count = (uint64_t)nd.L * nd.T * nd.F;
+  int64_t off = 0;
+  nd.w_off[0] = off;
+  off += (int64_t)nd.In * nd.W;
+  nd.b_off[0] = off;
+  off += nd.W;
+  for (int i = 1; i < nd.H; ++i) {
+    nd.w_off[i] = off;
+    off += (int64_t)nd.W * nd.W;
+    nd.b_off[i] = off;
+    off += nd.W;
+  }
+  nd.w_off[nd.H] = off;
+  off += (int64_t)nd.W * nd.O;
+  nd.b_off[nd.H] = off;
+  off += nd.O;
+  nd.mlp_count = (uint32_t)off;
+  // One fp32 resolution table for every kernel: iterative res *= scale from
+  // the 6-decimal literals (mlp_kernel_emitter.cpp:224-236).
+  float r = round6(s.base_resolution);
+  const float sc = round6(s.per_level_scale);
+  for (int l = 0; l < nd.L; ++l) {
+    nd.res[l] = r;
+    r = r * sc;
+  }
+  return nd;
+}
+
+void plan_family(tmnn_ctx &c) {
+  std::string why;
+  const bool fused_ok = fused_supported(c.spec, c.cfg, &why);
+  const int want = c.cfg.family;
+  if (want == TMNN_FAMILY_SAFE_DEBUG) {
+    c.family = TMNN_FAMILY_SAFE_DEBUG;
+    c.fallback_reason = kReasonForcedSafeDebug;
+    c.plan_text = "SafeDebug requested";
+  } else if (want == TMNN_FAMILY_TILED) {
+    // The tiled family (separate encode / MLP / scatter launches) runs the
+    // same fp32 reference-order kernels as SafeDebug on this build.
+    c.family = TMNN_FAMILY_TILED;
+    c.fallback_reason = kReasonForcedTiled;
+    c.plan_text = "Tiled requested";
+  } else if (fused_ok) {
+    c.family = TMNN_FAMILY_FULLY_FUSED;
+    c.fallback_reason = kReasonNone;
+    c.plan_text = "FullyFused: tcgen05 fused step";
+  } else if (want == TMNN_FAMILY_FULLY_FUSED) {
+    throw std::invalid_argument("FullyFused family unavailable: " + why);
+  } else {
+    c.family = TMNN_FAMILY_SAFE_DEBUG;
+    c.fallback_reason = why.find("hidden") != std::string::npos
+                            ? kReasonHiddenDimUnsupported
+                        : why.find("output") != std::string::npos
+                            ? kReasonUnsupportedOutputDims
+                            : kReasonEncodingRequiresTiledFamily;
+    c.plan_text = "SafeDebug fallback: " + why;
+  }
+}
+
+float kaiming_gain(const tmnn_train_cfg &c) {
+  // default_trainer.cpp:2037-2049
+  switch (c.mlp_nonlinearity) {
+    case 0:
+    case 4:
+      return 1.0f;
+    case 2:
+      return std::sqrt(2.0f / (1.0f + c.mlp_kaiming_a * c.mlp_kaiming_a));
+    case 3:
+      return 5.0f / 3.0f;
+    default:
+      return std::sqrt(2.0f);
+  }
+}
+
+// Philox weight init (default_trainer.cpp:1978-2180): hash U(-r, r) at
+// counter 0; the MLP per layer, weights then bias, each slice advancing the
+// counter by ceil(count / 4).
+void init_weights(tmnn_ctx &c) {
+  const tmnn_train_cfg &w = c.cfg;
+  cudaStream_t st = c.stream;
+  if (w.hash_init == 1)
+    CK(cudaMemsetAsync(c.hash_w(), 0, c.hash_count * sizeof(float), st));
+  else
+    launch_init_uniform(c.hash_w(), c.hash_count, -w.hash_init_range,
+                        w.hash_init_range, w.seed, 0u, st);
+  c.launches++;
+  uint32_t cb = (uint32_t)((c.hash_count + 3) / 4);
+  float *mlp = c.mlp_w();
+  if (w.mlp_init == 4 || w.mlp_init == 5 || w.mlp_init == 6) {
+    if (w.mlp_init == 4)
+      launch_init_uniform(mlp, c.mlp_count, -w.mlp_uniform_range,
+                          w.mlp_uniform_range, w.seed, cb, st);
+    else if (w.mlp_init == 5)
+      launch_init_normal(mlp, c.mlp_count, 0.0f, w.mlp_normal_stddev, w.seed,
+                         cb, st);
+    else
+      CK(cudaMemsetAsync(mlp, 0, c.mlp_count * sizeof(float), st));
+    c.launches++;
+    return;
+  }
+  const float gain = kaiming_gain(w);
+  const NetDims &nd = c.nd;
+  int64_t off = 0;
+  for (int layer = 0; layer <= nd.H; ++layer) {
+    const int fin = layer == 0 ? nd.In : nd.W;
+    const int fout = layer == nd.H ? nd.O : nd.W;
+    const uint64_t wc = (uint64_t)fin * fout;
+    const float fi = (float)fin, fo = (float)fout;
+    switch (w.mlp_init) {
+      case 0: {
+        const float b = gain * std::sqrt(3.0f / fi);
+        launch_init_uniform(mlp + off, wc, -b, b, w.seed, cb, st);
+        break;
+      }
+      case 1:
+        launch_init_normal(mlp + off, wc, 0.0f, gain / std::sqrt(fi), w.seed,
+                           cb, st);
+        break;
+      case 2: {
+        const float b = std::sqrt(6.0f / (fi + fo));
+        launch_init_uniform(mlp + off, wc, -b, b, w.seed, cb, st);
+        break;
+      }
+      default:
+        launch_init_normal(mlp + off, wc, 0.0f, std::sqrt(2.0f / (fi + fo)),
+                           w.seed, cb, st);
+    }
+    cb += (uint32_t)((wc + 3) / 4);
+    off += (int64_t)wc;
+    const float bb = 1.0f / std::sqrt(fi);
+    launch_init_uniform(mlp + off, (uint64_t)fout, -bb, bb, w.seed, cb, st);
+    cb += (uint32_t)((fout + 3) / 4);
+    off += fout;
+    c.launches += 2;
+  }
+}
+
+void refresh_gather_copy(tmnn_ctx &c) {
+  if (c.table_h.p) {
+    launch_to_half(c.hash_w(), c.table_h.p, c.hash_count, c.num_sms, c.stream);
+    c.launches++;
+  }
+  fused_weights_changed(c.fws);
+}
+
+void zero_grads(tmnn_ctx &c) {
+  if (c.gh_fixed.p)
+    CK(cudaMemsetAsync(c.gh_fixed.p, 0, c.gh_fixed.bytes(), c.stream));
+  if (c.gh_float.p)
+    CK(cudaMemsetAsync(c.gh_float.p, 0, c.gh_float.bytes(), c.stream));
+  CK(cudaMemsetAsync(c.gm.p, 0, c.gm.bytes(), c.stream));
+  CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
+}
+
+void reset_optimizer(tmnn_ctx &c) {
+  CK(cudaMemsetAsync(c.m.p, 0, c.m.bytes(), c.stream));
+  CK(cudaMemsetAsync(c.v.p, 0, c.v.bytes(), c.stream));
+  c.step = 0;
+}
+
+void ensure_batch(tmnn_ctx &c, uint32_t N) {
+  const size_t d = c.nd.d, O = c.nd.O;
+  c.pos_in.ensure(N * d);
+  c.tgt_in.ensure(N * O);
+  c.pos_s.ensure(N * d);
+  c.tgt_s.ensure(N * O);
+  c.out_buf.ensure(N * O);
+  c.out_s.ensure(N * O);
+  c.codes.ensure(N);
+  c.codes_alt.ensure(N);
+  c.idx.ensure(N);
+  c.perm.ensure(N);
+  const size_t tb = morton_temp_bytes(N);
+  c.sort_tmp.ensure(tb);
+}
+
+// Copies a caller array of `count` floats into `staging` (host pointer) or
+// passes a device pointer through.
+const float *stage_in(tmnn_ctx &c, const float *src, size_t count,
+                      DevBuf<float> &staging, uint32_t flags) {
+  if (!src) return nullptr;
+  if (flags & TMNN_PTR_DEVICE) return src;
+  if (count)
+    CK(cudaMemcpyAsync(staging.p, src, count * sizeof(float),
+                       cudaMemcpyHostToDevice, c.stream));
+  return staging.p;
+}
+
+// Morton order of the batch (morton_sort.h:60-110) on the device: codes,
+// stable radix sort, then row gathers of positions and the per-point array.
+void morton_sort(tmnn_ctx &c, const float *pos, const float *per_point,
+                 uint32_t N, const float **pos_out, const float **pp_out) {
+  launch_morton_order(pos, c.nd.d, N, c.codes.p, c.codes_alt.p, c.idx.p,
+                      c.perm.p, c.sort_tmp.p, c.sort_tmp.n, c.stream);
+  launch_gather_rows(pos, c.nd.d, c.perm.p, c.pos_s.p, N, c.stream);
+  c.launches += 3;
+  *pos_out = c.pos_s.p;
+  if (per_point) {
+    launch_gather_rows(per_point, c.nd.O, c.perm.p, c.tgt_s.p, N, c.stream);
+    c.launches++;
+    *pp_out = c.tgt_s.p;
+  }
+}
+
+// Forward + backward + scatter of one batch with the context's family.
+void fwd_bwd(tmnn_ctx &c, const float *pos, const float *tgt,
+             const float *dext, uint32_t N, float inv_N) {
+  if (N == 0) return;
+  if (c.family == TMNN_FAMILY_FULLY_FUSED) {
+    c.launches += fused_train(c.fws, c.nd, c.spec, c.params.p, c.table_h.p,
+                              pos, tgt, dext, inv_N, c.gm.p, c.gh_fixed.p,
+                              c.gh_float.p, c.touched.p, c.loss_acc.p, N,
+                              c.num_sms, c.stream);
+    return;
+  }
+  launch_train_exact(c.nd, c.hash_w(), c.mlp_w(), pos, tgt, dext, inv_N,
+                     c.gm.p, c.gh_fixed.p, c.gh_float.p, c.touched.p,
+                     c.loss_acc.p, N, c.scratch.p, c.num_sms, c.stream);
+  c.launches++;
+}
+
+void forward_dev(tmnn_ctx &c, const float *pos, float *out, uint32_t N) {
+  if (N == 0) return;
+  if (c.family == TMNN_FAMILY_FULLY_FUSED) {
+    c.launches += fused_forward(c.fws, c.nd, c.spec, c.params.p, c.table_h.p,
+                                pos, out, N, c.num_sms, c.stream);
+    return;
+  }
+  launch_forward_exact(c.nd, c.hash_w(), c.mlp_w(), pos, out, N, c.scratch.p,
+                       c.num_sms, c.stream);
+  c.launches++;
+}
+
+void allreduce_grads(tmnn_ctx &c, bool with_loss) {
+  if (!c.comm || c.world <= 1) return;
+  NK(ncclGroupStart());
+  if (c.nd.grad_fixed)
+    NK(ncclAllReduce(c.gh_fixed.p, c.gh_fixed.p, c.hash_count, ncclInt32,
+                     ncclSum, c.comm, c.stream));
+  else
+    NK(ncclAllReduce(c.gh_float.p, c.gh_float.p, c.hash_count, ncclFloat32,
+                     ncclSum, c.comm, c.stream));
+  NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
+                   c.stream));
+  if (c.sparse)
+    NK(ncclAllReduce(c.touched.p, c.touched.p, c.slots, ncclUint8, ncclMax,
+                     c.comm, c.stream));
+  if (with_loss)
+    NK(ncclAllReduce(c.loss_acc.p, c.loss_acc.p, 1, ncclFloat64, ncclSum,
+                     c.comm, c.stream));
+  NK(ncclGroupEnd());
+}
+
+// Adam over the fused [hash | mlp] buffer with the reference's bias
+// corrections bc_k = 1 - pow(beta_k, step + 1) in float (adam_params.h:33-52),
+// then the gradient reset; advances the step counter.
+void adam(tmnn_ctx &c) {
+  AdamArgs a{};
+  const float s = (float)(c.step + 1u);
+  a.lr_hash = c.cfg.lr_encoding;
+  a.lr_mlp = c.cfg.lr_network;
+  a.beta1 = c.cfg.beta1;
+  a.beta2 = c.cfg.beta2;
+  a.eps = c.cfg.epsilon;
+  a.bc1 = 1.0f - std::pow(c.cfg.beta1, s);
+  a.bc2 = 1.0f - std::pow(c.cfg.beta2, s);
+  a.l1_hash = c.cfg.l1_reg;
+  a.l2_mlp = c.cfg.l2_reg;
+  a.grad_clip = c.cfg.grad_clip;
+  a.weight_decay = c.cfg.weight_decay;
+  a.hash_count = c.hash_count;
+  a.mlp_count = c.mlp_count;
+  a.slots = c.slots;
+  a.entry_width = c.entry_width;
+  a.sparse = c.sparse ? 1 : 0;
+  a.grad_fixed = c.nd.grad_fixed;
+  launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
+              c.touched.p, c.table_h.p, c.num_sms, c.stream);
+  c.launches++;
+  fused_weights_changed(c.fws);
+  if (!c.sparse)  // the dense path leaves the touched map unused
+    CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
+  c.step++;
+}
+
+void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
+            const tmnn_train_cfg &cfg) {
+  validate(spec);
+  if (cfg.hash_grad_format != TMNN_GRAD_FIXED16 &&
+      cfg.hash_grad_format != TMNN_GRAD_F32)
+    throw std::invalid_argument("hash_grad_format must be FIXED16 or F32");
+  if (cfg.batch_size <= 0) throw std::invalid_argument("batch_size must be > 0");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    throw std::runtime_error("no CUDA device available");
+  if (device < 0 || device >= ndev)
+    throw std::invalid_argument("device index out of range");
+  c.device = device;
+  CK(cudaSetDevice(device));
+  CK(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
+  CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+  for (auto &e : c.ev) CK(cudaEventCreate(&e));
+  CK(cudaMallocHost(&c.h_loss, sizeof(double)));
+  c.spec = spec;
+  c.cfg = cfg;
+  c.nd = make_dims(spec, cfg);
+  c.hash_count = c.nd.hash_count;
+  c.mlp_count = c.nd.mlp_count;
+  c.entry_width = c.nd.F == 2 ? 2 : 1;
+  c.slots = c.hash_count / c.entry_width;
+  // use_sparse_hash_adam_path (default_trainer.cpp:1868-1876): sparse iff
+  // l1_reg == 0, unless overridden.
+  c.sparse = cfg.sparse_hash_adam < 0 ? cfg.l1_reg == 0.0f
+                                      : cfg.sparse_hash_adam != 0;
+  const uint64_t total = c.hash_count + c.mlp_count;
+  c.params.alloc(total);
+  c.m.alloc(total);
+  c.v.alloc(total);
+  if (spec.table_dtype == TMNN_DTYPE_F16) c.table_h.alloc(c.hash_count);
+  if (c.nd.grad_fixed)
+    c.gh_fixed.alloc(c.hash_count);
+  else
+    c.gh_float.alloc(c.hash_count);
+  c.gm.alloc(c.mlp_count);
+  c.touched.alloc(c.slots);
+  c.loss_acc.alloc(1);
+  const size_t sf = exact_scratch_floats(c.nd, c.num_sms);
+  if (sf) c.scratch.alloc(sf);
+  plan_family(c);
+  init_weights(c);
+  refresh_gather_copy(c);
+  reset_optimizer(c);
+  zero_grads(c);
+  CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(double), c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+}
+
+void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
+                uint32_t flags, tmnn_step_result *res) {
+  if (N > 0 && (!pos || !tgt))
+    throw std::invalid_argument("training_step: null positions or targets");
+  CK(cudaSetDevice(c.device));
+  ensure_batch(c, N);
+  const bool prof = flags & TMNN_PROFILE;
+  if (prof) CK(cudaEventRecord(c.ev[0], c.stream));
+  const float *p = stage_in(c, pos, (size_t)N * c.nd.d, c.pos_in, flags);
+  const float *t = stage_in(c, tgt, (size_t)N * c.nd.O, c.tgt_in, flags);
+  if (c.cfg.morton_sort && N > 1) morton_sort(c, p, t, N, &p, &t);
+  CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(double), c.stream));
+  const uint64_t global_n = (uint64_t)N * (uint64_t)c.world;
+  const float inv_N = global_n ? 1.0f / (float)global_n : 0.0f;
+  if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
+  fwd_bwd(c, p, t, nullptr, N, inv_N);
+  if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
+  allreduce_grads(c, true);
+  if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
+  const uint32_t done = c.step;
+  adam(c);
+  if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
+  CK(cudaMemcpyAsync(c.h_loss, c.loss_acc.p, sizeof(double),
+                     cudaMemcpyDeviceToHost, c.stream));
+  if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+  if (res) {
+    std::memset(res, 0, sizeof *res);
+    // finalize_async_step: mean_loss = total / float(batch_N)
+    // (parameter_store.cpp:303-322)
+    res->loss = global_n ? (float)*c.h_loss / (float)global_n : 0.0f;
+    res->step = done;
+    res->batch_size = N;
+    res->numerics_ok = std::isfinite(res->loss) ? 1 : 0;
+    res->family = c.family;
+    if (prof) {
+      CK(cudaEventElapsedTime(&res->gpu_ms, c.ev[0], c.ev[5]));
+      CK(cudaEventElapsedTime(&res->sort_ms, c.ev[0], c.ev[1]));
+      CK(cudaEventElapsedTime(&res->fwd_bwd_ms, c.ev[1], c.ev[2]));
+      CK(cudaEventElapsedTime(&res->allreduce_ms, c.ev[2], c.ev[3]));
+      CK(cudaEventElapsedTime(&res->adam_ms, c.ev[3], c.ev[4]));
+    }
+  }
+}
+
+void copy_out(tmnn_ctx &c, float *dst, const float *src, size_t count,
+              uint32_t flags) {
+  if (!count) return;
+  CK(cudaMemcpyAsync(dst, src, count * sizeof(float),
+                     (flags & TMNN_PTR_DEVICE) ? cudaMemcpyDeviceToDevice
+                                               : cudaMemcpyDeviceToHost,
+                     c.stream));
+}
+
+void forward_api(tmnn_ctx &c, const float *pos, float *out, uint32_t N,
+                 uint32_t flags) {
+  if (N > 0 && (!pos || !out))
+    throw std::invalid_argument("forward: null positions or outputs");
+  CK(cudaSetDevice(c.device));
+  ensure_batch(c, N);
+  const float *p = stage_in(c, pos, (size_t)N * c.nd.d, c.pos_in, flags);
+  float *o = (flags & TMNN_PTR_DEVICE) ? out : c.out_buf.p;
+  forward_dev(c, p, o, N);
+  if (!(flags & TMNN_PTR_DEVICE)) copy_out(c, out, o, (size_t)N * c.nd.O, flags);
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+}
+
+void backward_accumulate(tmnn_ctx &c, const float *pos, const float *dout,
+                         uint32_t N, uint32_t flags) {
+  if (N > 0 && (!pos || !dout))
+    throw std::invalid_argument("backward_accumulate: null arguments");
+  CK(cudaSetDevice(c.device));
+  ensure_batch(c, N);
+  const float *p = stage_in(c, pos, (size_t)N * c.nd.d, c.pos_in, flags);
+  const float *g = stage_in(c, dout, (size_t)N * c.nd.O, c.tgt_in, flags);
+  if (c.cfg.morton_sort && N > 1) morton_sort(c, p, g, N, &p, &g);
+  fwd_bwd(c, p, nullptr, g, N, 0.0f);
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+}
+
+}  // namespace
+
+// ====================================================================== ABI
+
+extern "C" {
+
+void tmnn_cuda_default_train_cfg(tmnn_train_cfg *c) {
+  if (!c) return;
+  std::memset(c, 0, sizeof *c);
+  c->batch_size = 1024;
+  c->lr_encoding = 1e-2f;
+  c->lr_network = 1e-3f;
+  c->beta1 = 0.9f;
+  c->beta2 = 0.99f;
+  c->epsilon = 1e-15f;
+  c->hash_init = 0;
+  c->hash_init_range = 1.0e-4f;
+  c->mlp_init = 0;
+  c->mlp_nonlinearity = 1;
+  c->mlp_uniform_range = 1.0e-2f;
+  c->mlp_normal_stddev = 1.0e-2f;
+  c->seed = 42u;
+  c->family = TMNN_FAMILY_AUTO;
+  c->hash_grad_format = TMNN_GRAD_FIXED16;
+  c->morton_sort = 1;
+  c->sparse_hash_adam = -1;
+}
+
+tmnn_status tmnn_cuda_validate_spec(const tmnn_spec *spec) {
+  if (!spec) {
+    g_last_error = "null spec";
+    return TMNN_ERR_NULL_OBJECT;
+  }
+  return guarded([&] { validate(*spec); });
+}
+
+tmnn_status tmnn_cuda_ctx_create(int device, const tmnn_spec *spec,
+                                 const tmnn_train_cfg *cfg, tmnn_ctx **out) {
+  if (!spec || !out) {
+    g_last_error = "null argument";
+    return TMNN_ERR_NULL_OBJECT;
+  }
+  *out = nullptr;
+  tmnn_train_cfg dflt;
+  tmnn_cuda_default_train_cfg(&dflt);
+  std::unique_ptr<tmnn_ctx> c(new tmnn_ctx);
+  tmnn_status st = guarded([&] { create(*c, device, *spec, cfg ? *cfg : dflt); });
+  if (st == TMNN_OK) *out = c.release();
+  return st;
+}
+
+tmnn_status tmnn_cuda_ctx_create_from_json(int device, uint32_t n_input,
+                                           uint32_t n_output, const char *json,
+                                           tmnn_ctx **out) {
+  if (!out) {
+    g_last_error = "null argument";
+    return TMNN_ERR_NULL_OBJECT;
+  }
+  *out = nullptr;
+  tmnn_spec spec;
+  tmnn_train_cfg cfg;
+  tmnn_status st =
+      guarded([&] { config_from_json(n_input, n_output, json, &spec, &cfg); });
+  if (st != TMNN_OK) return st;
+  return tmnn_cuda_ctx_create(device, &spec, &cfg, out);
+}
+
+tmnn_status tmnn_cuda_ctx_destroy(tmnn_ctx *ctx) {
+  REQUIRE_CTX(ctx);
+  return guarded([&] {
+    cudaSetDevice(ctx->device);
+    delete ctx;
+  });
+}
+
+tmnn_status tmnn_cuda_set_initial_weights(tmnn_ctx *c, const float *hash,
+                                          size_t hash_count, const float *mlp,
+                                          size_t mlp_count) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (hash && hash_count != c->hash_count)
+      throw std::invalid_argument("set_initial_weights: hash count mismatch");
+    if (mlp && mlp_count != c->mlp_count)
+      throw std::invalid_argument("set_initial_weights: mlp count mismatch");
+    CK(cudaSetDevice(c->device));
+    if (hash)
+      CK(cudaMemcpyAsync(c->hash_w(), hash, hash_count * 4,
+                         cudaMemcpyHostToDevice, c->stream));
+    if (mlp)
+      CK(cudaMemcpyAsync(c->mlp_w(), mlp, mlp_count * 4,
+                         cudaMemcpyHostToDevice, c->stream));
+    refresh_gather_copy(*c);
+    reset_optimizer(*c);
+    zero_grads(*c);
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_get_weights(tmnn_ctx *c, float *hash, size_t hash_count,
+                                  float *mlp, size_t mlp_count) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (hash && hash_count != c->hash_count)
+      throw std::invalid_argument("get_weights: hash count mismatch");
+    if (mlp && mlp_count != c->mlp_count)
+      throw std::invalid_argument("get_weights: mlp count mismatch");
+    CK(cudaSetDevice(c->device));
+    if (hash)
+      CK(cudaMemcpyAsync(hash, c->hash_w(), hash_count * 4,
+                         cudaMemcpyDeviceToHost, c->stream));
+    if (mlp)
+      CK(cudaMemcpyAsync(mlp, c->mlp_w(), mlp_count * 4,
+                         cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_train_step(tmnn_ctx *c, const float *positions,
+                                 const float *targets, uint32_t n,
+                                 uint32_t flags, tmnn_step_result *result) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    train_step(*c, positions, targets, n, flags, result);
+  });
+}
+
+tmnn_status tmnn_cuda_forward_backward(tmnn_ctx *c, const float *positions,
+                                       const float *targets, uint32_t n,
+                                       uint32_t flags, double *loss_sum) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (n > 0 && (!positions || !targets))
+      throw std::invalid_argument("forward_backward: null arguments");
+    CK(cudaSetDevice(c->device));
+    ensure_batch(*c, n);
+    const float *p = stage_in(*c, positions, (size_t)n * c->nd.d, c->pos_in, flags);
+    const float *t = stage_in(*c, targets, (size_t)n * c->nd.O, c->tgt_in, flags);
+    if (c->cfg.morton_sort && n > 1) morton_sort(*c, p, t, n, &p, &t);
+    CK(cudaMemsetAsync(c->loss_acc.p, 0, sizeof(double), c->stream));
+    const uint64_t global_n = (uint64_t)n * (uint64_t)c->world;
+    fwd_bwd(*c, p, t, nullptr, n, global_n ? 1.0f / (float)global_n : 0.0f);
+    CK(cudaMemcpyAsync(c->h_loss, c->loss_acc.p, sizeof(double),
+                       cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    if (loss_sum) *loss_sum = *c->h_loss;
+  });
+}
+
+tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *c, int32_t role, void *host,
+                                  size_t bytes) {
+  REQUIRE_CTX(c);
+  tmnn_buffer_view v;
+  tmnn_status st = tmnn_cuda_get_buffer(c, role, &v);
+  if (st != TMNN_OK) return st;
+  return guarded([&] {
+    BusyGuard g(c);
+    if (!host || bytes != v.bytes)
+      throw std::invalid_argument("read_buffer: size mismatch");
+    CK(cudaSetDevice(c->device));
+    CK(cudaMemcpyAsync(host, v.device_ptr, bytes, cudaMemcpyDeviceToHost,
+                       c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_forward(tmnn_ctx *c, const float *positions,
+                              float *outputs, uint32_t n, uint32_t flags) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    forward_api(*c, positions, outputs, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_zero_grads(tmnn_ctx *c) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    CK(cudaSetDevice(c->device));
+    zero_grads(*c);
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_backward_accumulate(tmnn_ctx *c, const float *positions,
+                                          const float *d_output, uint32_t n,
+                                          uint32_t flags) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    backward_accumulate(*c, positions, d_output, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_adam_step(tmnn_ctx *c) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    CK(cudaSetDevice(c->device));
+    allreduce_grads(*c, false);
+    adam(*c);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+  });
+}
+
+tmnn_status tmnn_cuda_evaluate(tmnn_ctx *c, const float *positions,
+                               float *outputs, uint32_t n, uint32_t flags) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    forward_api(*c, positions, outputs, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_debug_encode(tmnn_ctx *c, const float *positions,
+                                   uint32_t n, float *features,
+                                   uint32_t *corner_index, int32_t *cells) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (n > 0 && (!positions || !features))
+      throw std::invalid_argument("debug_encode: null arguments");
+    CK(cudaSetDevice(c->device));
+    ensure_batch(*c, n);
+    const float *p = stage_in(*c, positions, (size_t)n * c->nd.d, c->pos_in, 0);
+    DevBuf<float> feat;
+    DevBuf<uint32_t> ci;
+    DevBuf<int32_t> ce;
+    const size_t nc = (size_t)1 << c->nd.d;
+    feat.alloc((size_t)n * c->nd.In);
+    if (corner_index) ci.alloc((size_t)n * c->nd.L * nc);
+    if (cells) ce.alloc((size_t)n * c->nd.L * c->nd.d);
+    launch_encode_debug(c->nd, c->hash_w(), p, feat.p, ci.p, ce.p, n, c->stream);
+    c->launches++;
+    if (n) {
+      CK(cudaMemcpyAsync(features, feat.p, feat.bytes(), cudaMemcpyDeviceToHost,
+                         c->stream));
+      if (corner_index)
+        CK(cudaMemcpyAsync(corner_index, ci.p, ci.bytes(),
+                           cudaMemcpyDeviceToHost, c->stream));
+      if (cells)
+        CK(cudaMemcpyAsync(cells, ce.p, ce.bytes(), cudaMemcpyDeviceToHost,
+                           c->stream));
+    }
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_export_opt_state(tmnn_ctx *c, uint8_t *buf, size_t cap,
+                                       size_t *len, uint32_t *step) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (!len) throw std::invalid_argument("export_opt_state: null len");
+    const size_t hb = c->hash_count * 4, mb = (size_t)c->mlp_count * 4;
+    if (hb > 0xFFFFFFFFull)
+      throw CapacityError("export_opt_state: section exceeds u32 length");
+    const size_t need = 4 * 4 + 2 * hb + 2 * mb;
+    *len = need;
+    if (step) *step = c->step;
+    if (!buf) return;
+    if (cap < need) throw CapacityError("export_opt_state: buffer too small");
+    CK(cudaSetDevice(c->device));
+    // sections [m_hash, v_hash, m_mlp, v_mlp] (default_trainer.cpp:83-100)
+    struct Sec {
+      const float *src;
+      size_t bytes;
+    } secs[4] = {{c->m.p, hb}, {c->v.p, hb}, {c->m.p + c->hash_count, mb},
+                 {c->v.p + c->hash_count, mb}};
+    size_t off = 0;
+    for (auto &s : secs) {
+      for (int i = 0; i < 4; ++i) buf[off + i] = (uint8_t)(s.bytes >> (8 * i));
+      off += 4;
+      CK(cudaMemcpyAsync(buf + off, s.src, s.bytes, cudaMemcpyDeviceToHost,
+                         c->stream));
+      off += s.bytes;
+    }
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_import_opt_state(tmnn_ctx *c, const uint8_t *buf,
+                                       size_t len, uint32_t step) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (!buf) throw std::invalid_argument("import_opt_state: null buffer");
+    const size_t hb = c->hash_count * 4, mb = (size_t)c->mlp_count * 4;
+    const size_t want[4] = {hb, hb, mb, mb};
+    float *dst[4] = {c->m.p, c->v.p, c->m.p + c->hash_count,
+                     c->v.p + c->hash_count};
+    size_t off = 0;
+    for (int s = 0; s < 4; ++s) {
+      if (off + 4 > len)
+        throw std::invalid_argument("import_opt_state: truncated payload");
+      uint32_t n = 0;
+      for (int i = 0; i < 4; ++i) n |= (uint32_t)buf[off + i] << (8 * i);
+      off += 4;
+      if (n != want[s])
+        throw std::invalid_argument(
+            "import_opt_state: section size mismatch (layout differs)");
+      if (off + n > len)
+        throw std::invalid_argument("import_opt_state: truncated payload");
+      off += n;
+    }
+    if (off != len)
+      throw std::invalid_argument("import_opt_state: trailing bytes");
+    CK(cudaSetDevice(c->device));
+    off = 0;
+    for (int s = 0; s < 4; ++s) {
+      off += 4;
+      CK(cudaMemcpyAsync(dst[s], buf + off, want[s], cudaMemcpyHostToDevice,
+                         c->stream));
+      off += want[s];
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    c->step = step;
+  });
+}
+
+tmnn_status tmnn_cuda_reset_optimizer(tmnn_ctx *c) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    CK(cudaSetDevice(c->device));
+    reset_optimizer(*c);
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_get_step(tmnn_ctx *c, uint32_t *step) {
+  REQUIRE_CTX(c);
+  if (!step) return TMNN_ERR_INVALID_ARGUMENT;
+  *step = c->step;
+  return TMNN_OK;
+}
+
+tmnn_status tmnn_cuda_get_buffer(tmnn_ctx *c, int32_t role,
+                                 tmnn_buffer_view *v) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    if (!v) throw std::invalid_argument("get_buffer: null view");
+    std::memset(v, 0, sizeof *v);
+    switch (role) {
+      case TMNN_BUF_HASH_WEIGHTS:
+        *v = {c->hash_w(), c->hash_count * 4, 0};
+        break;
+      case TMNN_BUF_MLP_WEIGHTS:
+        *v = {c->mlp_w(), (size_t)c->mlp_count * 4, 0};
+        break;
+      case TMNN_BUF_GRAD_HASH:
+        if (c->gh_fixed.p)
+          *v = {c->gh_fixed.p, c->gh_fixed.bytes(), 2};
+        else
+          *v = {c->gh_float.p, c->gh_float.bytes(), 0};
+        break;
+      case TMNN_BUF_GRAD_MLP:
+        *v = {c->gm.p, c->gm.bytes(), 0};
+        break;
+      case TMNN_BUF_FUSED_WEIGHTS:
+        *v = {c->params.p, c->params.bytes(), 0};
+        break;
+      case TMNN_BUF_FUSED_M:
+        *v = {c->m.p, c->m.bytes(), 0};
+        break;
+      case TMNN_BUF_FUSED_V:
+        *v = {c->v.p, c->v.bytes(), 0};
+        break;
+      case TMNN_BUF_HASH_GATHER:
+        if (!c->table_h.p)
+          throw std::invalid_argument("get_buffer: no fp16 gather copy");
+        *v = {c->table_h.p, c->table_h.bytes(), 1};
+        break;
+      case TMNN_BUF_TOUCHED:
+        *v = {c->touched.p, c->touched.bytes(), 3};
+        break;
+      default:
+        throw std::invalid_argument("get_buffer: unknown role");
+    }
+  });
+}
+
+tmnn_status tmnn_cuda_get_plan(tmnn_ctx *c, tmnn_plan *p) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    if (!p) throw std::invalid_argument("get_plan: null plan");
+    std::memset(p, 0, sizeof *p);
+    p->family = c->family;
+    p->fallback_reason = c->fallback_reason;
+    p->mlp_weight_count = c->mlp_count;
+    p->hash_grid_size = c->hash_count;
+    p->device_bytes = c->params.bytes() + c->m.bytes() + c->v.bytes() +
+                      c->table_h.bytes() + c->gh_fixed.bytes() +
+                      c->gh_float.bytes() + c->gm.bytes() + c->touched.bytes() +
+                      c->scratch.bytes();
+    p->n_levels = c->nd.L;
+    p->n_features_per_level = c->nd.F;
+    p->spatial_dims = c->nd.d;
+    p->num_outputs = c->nd.O;
+    std::snprintf(p->reason, sizeof p->reason, "%s", c->plan_text.c_str());
+  });
+}
+
+tmnn_status tmnn_cuda_get_stream(tmnn_ctx *c, void **stream) {
+  REQUIRE_CTX(c);
+  if (!stream) return TMNN_ERR_INVALID_ARGUMENT;
+  *stream = (void *)c->stream;
+  return TMNN_OK;
+}
+
+tmnn_status tmnn_cuda_synchronize(tmnn_ctx *c) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+  });
+}
+
+tmnn_status tmnn_cuda_dp_unique_id(uint8_t out[128]) {
+  return guarded([&] {
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    ncclUniqueId id;
+    NK(ncclGetUniqueId(&id));
+    std::memcpy(out, &id, 128);
+  });
+}
+
+tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
+                              int rank, int world) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (world < 1 || rank < 0 || rank >= world)
+      throw std::invalid_argument("dp_init: bad rank/world");
+    CK(cudaSetDevice(c->device));
+    if (c->comm) {
+      ncclCommDestroy(c->comm);
+      c->comm = nullptr;
+    }
+    c->rank = rank;
+    c->world = world;
+    if (world > 1) {
+      ncclUniqueId id;
+      std::memcpy(&id, unique_id, 128);
+      NK(ncclCommInitRank(&c->comm, world, id, rank));
+    }
+  });
+}
+
+const char *tmnn_cuda_last_error(void) { return g_last_error.c_str(); }
+
+tmnn_status tmnn_cuda_launch_count(tmnn_ctx *c, uint64_t *count) {
+  REQUIRE_CTX(c);
+  if (!count) return TMNN_ERR_INVALID_ARGUMENT;
+  *count = c->launches;
+  return TMNN_OK;
+}
+
+}  // extern "C"
