@@ -274,7 +274,8 @@ class OracleTrainer:
 
     def training_step(self, pos, tgt):
         pos = np.ascontiguousarray(pos, np.float32)
-        tgt = np.ascontiguousarray(tgt, np.float32).reshape(pos.shape[0], -1)
+        tgt = np.ascontiguousarray(tgt, np.float32).reshape(pos.shape[0],
+                                                             self.s.O)
         if self.morton and pos.shape[0] > 1:
             perm = morton_order(pos)
             pos, tgt = pos[perm], tgt[perm]

@@ -1,0 +1,139 @@
+"""FullyFused family (tcgen05 MLP, fp16 operands, fp32 accumulation) against
+the CPU oracle.  Tolerance per the contract: MLP outputs and gradients within
+1e-2 relative (fp16 tensor-core math vs the fp32 reference), measured as
+max-abs error over the max magnitude (outputs) and as relative Frobenius
+norm (gradient tensors); the loss curve within 2 %."""
+import numpy as np
+import pytest
+
+import oracle as o
+from _util import batch, cuda_trainer, oracle_spec
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+CASES = [
+    dict(L=16, F=2, log2T=14, d=3, W=64, H=1, O=1, loss=1),   # SDF shape
+    dict(L=16, F=2, log2T=12, d=3, W=64, H=2, O=3, loss=0, scale=1.5),  # image
+    dict(L=16, F=2, log2T=12, d=4, W=64, H=2, O=4, loss=0, base=8.0, scale=1.5),
+    dict(L=16, F=1, log2T=12, d=3, W=64, H=1, O=1, loss=2, huber=0.1),
+    dict(L=4, F=4, log2T=12, d=3, W=64, H=3, O=2, loss=0),
+    dict(L=8, F=2, log2T=12, d=3, W=128, H=1, O=16, loss=0),
+    dict(L=8, F=2, log2T=12, d=3, W=64, H=4, O=3, loss=3),
+]
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def setup(kw, table="F32", grad="F32", seed=0, N=1000, scale_w=1.0):
+    tr = cuda_trainer(**kw, family="FullyFused", table=table, grad=grad,
+                      morton=False)
+    assert tr.plan()["family"] == "FullyFused"
+    rng = np.random.default_rng(seed)
+    hw = rng.uniform(-0.5, 0.5, tr.hash_count).astype(np.float32)
+    _, mw = tr.weights()
+    mw = (mw * scale_w).astype(np.float32)
+    tr.set_initial_weights(hw, mw)
+    lo = 0.0 if kw.get("d", 3) == 4 else -1.0
+    pos, tgt = batch(N, kw.get("d", 3), kw["O"], seed=seed + 1, lo=lo)
+    return tr, hw, mw, pos, tgt
+
+
+@pytest.mark.parametrize("kw", CASES)
+def test_fused_forward_matches_oracle(kw):
+    tr, hw, mw, pos, _ = setup(kw)
+    out = tr.inference(pos)
+    ref = o.forward(oracle_spec(**kw), hw, mw, pos)
+    assert np.abs(out - ref).max() <= TOL * max(np.abs(ref).max(), 1e-3)
+    tr.close()
+
+
+@pytest.mark.parametrize("kw", CASES)
+def test_fused_gradients_match_oracle(kw):
+    tr, hw, mw, pos, tgt = setup(kw)
+    if kw["loss"] == 3:
+        tgt = np.abs(tgt) + 0.1
+    lsum = tr.forward_backward(pos, tgt)
+    gh = tr.read_buffer(3)
+    gm = tr.read_buffer(4)
+    touched = tr.read_buffer(21)
+    s = oracle_spec(**kw, grad="F32")
+    lref, g, _ = o.fwd_bwd(s, hw, mw, pos, tgt)
+    assert abs(lsum - lref) <= TOL * abs(lref)
+    assert rel(gh, g["hash_float"]) <= TOL
+    assert rel(gm, g["mlp"]) <= TOL
+    assert np.array_equal(touched, g["touched"])
+    tr.close()
+
+
+def test_fused_fp16_table_and_fixed_point():
+    kw = CASES[0]
+    tr, hw, mw, pos, tgt = setup(kw, table="F16", grad="Fixed16", N=4000)
+    tr.forward_backward(pos, tgt)
+    gh = tr.read_buffer(3).astype(np.float64)
+    s = oracle_spec(**kw, grad="Fixed16")
+    hw16 = hw.astype(np.float16).astype(np.float32)
+    _, g, _ = o.fwd_bwd(s, hw16, mw, pos, tgt)
+    assert rel(gh, g["hash_fixed"].astype(np.float64)) <= 2 * TOL
+    out = tr.inference(pos)
+    ref = o.forward(oracle_spec(**kw), hw16, mw, pos)
+    assert np.abs(out - ref).max() <= TOL * np.abs(ref).max()
+    tr.close()
+
+
+@pytest.mark.parametrize("N", [0, 1, 127, 129, 3000])
+def test_fused_ragged_batches(N):
+    kw = dict(L=8, F=2, log2T=12, d=3, W=64, H=2, O=2, loss=0)
+    tr, hw, mw, pos, tgt = setup(kw, N=N)
+    lsum = tr.forward_backward(pos, tgt)
+    s = oracle_spec(**kw, grad="F32")
+    lref, g, _ = o.fwd_bwd(s, hw, mw, pos, tgt)
+    assert abs(lsum - lref) <= TOL * max(abs(lref), 1e-12)
+    if N:
+        assert rel(tr.read_buffer(4), g["mlp"]) <= TOL
+        assert rel(tr.read_buffer(3), g["hash_float"]) <= TOL
+    out = tr.inference(pos)
+    assert out.shape == (N, 2)
+    tr.close()
+
+
+def test_fused_external_gradient():
+    kw = dict(L=8, F=2, log2T=12, d=3, W=64, H=1, O=3, loss=0)
+    tr, hw, mw, pos, _ = setup(kw, N=2000)
+    d_out = (np.random.default_rng(5).normal(size=(2000, 3)) * 1e-3).astype(np.float32)
+    tr.zero_gradients()
+    tr.backward_accumulate(pos, d_out)
+    s = oracle_spec(**kw, grad="F32")
+    _, g, _ = o.fwd_bwd(s, hw, mw, pos, None, d_out=d_out)
+    assert rel(tr.read_buffer(3), g["hash_float"]) <= TOL
+    assert rel(tr.read_buffer(4), g["mlp"]) <= TOL
+    tr.close()
+
+
+def test_fused_loss_curve_within_2_percent():
+    """1000 steps of the SDF-shaped problem: the fused CUDA trainer and the
+    CPU oracle trainer, same seeds and batches; loss curves agree to 2 %
+    (averaged over the last 50 steps)."""
+    kw = dict(L=8, F=2, log2T=14, d=3, W=64, H=1, O=1, loss=1)
+    tr = cuda_trainer(**kw, family="FullyFused", grad="F32", lr_enc=1e-2,
+                      lr_net=1e-2)
+    hw, mw = tr.weights()
+    ot = o.OracleTrainer(oracle_spec(**kw, grad="F32"), hw, mw, lr_hash=1e-2,
+                         lr_mlp=1e-2, nthreads=0)
+    rng = np.random.default_rng(1234)
+    centers = rng.uniform(-0.6, 0.6, (8, 3)).astype(np.float32)
+    radii = rng.uniform(0.1, 0.4, 8).astype(np.float32)
+    la, lb = [], []
+    for s in range(1000):
+        pos = rng.uniform(-1, 1, (2048, 3)).astype(np.float32)
+        d = np.linalg.norm(pos[:, None] - centers[None], axis=2) - radii[None]
+        tgt = d.min(1, keepdims=True).astype(np.float32)
+        la.append(tr.training_step(pos, tgt))
+        lb.append(ot.training_step(pos, tgt))
+    a, b = np.mean(la[-50:]), np.mean(lb[-50:])
+    assert abs(a - b) <= 0.02 * b, (a, b)
+    assert a < 0.5 * np.mean(la[:10])
+    tr.close()

@@ -1,28 +1,851 @@
-// fused.cu -- FullyFused family (tcgen05).  Placeholder: not yet available.
+// fused.cu -- the FullyFused family: one persistent sm_100a kernel per
+// training step.  Each CTA (128 threads, one point per thread) loops over
+// 128-point tiles:
+//
+//   encode     thread t gathers the 2^d corners of every level for point t
+//              from the (fp16 or fp32) table and interpolates in fp32
+//              (mlp_kernel_emitter.cpp:205-360), writing fp16 features into
+//              a core-blocked shared tile X[128 x In];
+//   forward    D = X.W0, H_k = relu(D + b) ..., Y = H.Wout + bout on tcgen05
+//              (fp16 operands from shared memory, fp32 accumulators in TMEM;
+//              thread t reads TMEM lane t = point t in the epilogues);
+//   loss       L1/L2/Huber/Cosine per point (mlp_kernel_emitter.cpp:562-670);
+//              dY is scaled by a power of two so fp16 keeps its precision;
+//   backward   dH = (dY.Wout^T) o relu', ..., dX = dH0.W0^T on tcgen05; the
+//              weight gradients dW^T = dH^T.[H | 1] (the ones column yields
+//              the bias gradient) accumulate in TMEM across all tiles of the
+//              CTA and are flushed once with fp32 atomics;
+//   scatter    thread t recomputes its corners and adds d_feature * weight
+//              into the hash-gradient buffer with vector reductions
+//              (red.global.add.v2.f32 for two features) or the reference's
+//              int32 fixed point, and marks the touched slots.
+//
+// The same kernel without the backward half is the inference path.
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
 #include "fused.h"
+#include "tc.cuh"
 
 namespace tmnn {
+namespace {
 
-bool fused_supported(const tmnn_spec &, const tmnn_train_cfg &,
-                     std::string *why) {
-  if (why) *why = "fused tcgen05 kernel not built";
-  return false;
+constexpr int kTile = 128;
+constexpr int kThreads = 128;
+constexpr int kMaxTrainHidden = 4;
+constexpr int kOutCols = 16;  // output layer padded to N = 16
+constexpr uint32_t kWaitBound = 1u << 26;
+
+struct Layout {
+  // weight image (same bytes in global and shared memory)
+  uint32_t w[kMaxHidden + 1];  // W0, W1..W(H-1), Wout (core-blocked fp16)
+  uint32_t b[kMaxHidden + 1];  // fp32 biases (bout padded to 16)
+  uint32_t image_bytes;
+  // activation tiles
+  uint32_t x, h[kMaxHidden], dh[2], dy, misc;
+  uint32_t total;
+  int xc, hc;                  // stored columns of X and H tiles
+  int n_h_tiles;
+  // TMEM columns
+  uint32_t t_scratch, t_dw0, t_dwk[kMaxHidden], t_dwout, tmem_cols;
+};
+
+inline uint32_t align128(uint32_t v) { return (v + 127u) & ~127u; }
+
+Layout make_layout(const NetDims &nd, bool train) {
+  Layout L{};
+  const int In = nd.In, W = nd.W, H = nd.H;
+  uint32_t off = 0;
+  L.w[0] = off;
+  off = align128(off + In * W * 2);
+  for (int k = 1; k < H; ++k) {
+    L.w[k] = off;
+    off = align128(off + W * W * 2);
+  }
+  L.w[H] = off;
+  off = align128(off + W * kOutCols * 2);
+  for (int k = 0; k < H; ++k) {
+    L.b[k] = off;
+    off = align128(off + W * 4);
+  }
+  L.b[H] = off;
+  off = align128(off + kOutCols * 4);
+  L.image_bytes = off;
+  L.xc = train ? In + 16 : In;
+  L.hc = train ? W + 16 : W;
+  L.x = off;
+  off = align128(off + kTile * L.xc * 2);
+  L.n_h_tiles = train ? H : (H > 1 ? 2 : 1);
+  for (int k = 0; k < L.n_h_tiles; ++k) {
+    L.h[k] = off;
+    off = align128(off + kTile * L.hc * 2);
+  }
+  if (train) {
+    for (int k = 0; k < 2; ++k) {
+      L.dh[k] = off;
+      off = align128(off + kTile * W * 2);
+    }
+    L.dy = off;
+    off = align128(off + kTile * kOutCols * 2);
+  }
+  L.misc = off;
+  off = align128(off + 256);
+  L.total = off;
+  // TMEM
+  uint32_t col = 0;
+  L.t_scratch = col;
+  col += (uint32_t)(W > In ? W : In);
+  if (train) {
+    L.t_dw0 = col;
+    col += In + 16;
+    for (int k = 1; k < H; ++k) {
+      L.t_dwk[k] = col;
+      col += W + 16;
+    }
+    L.t_dwout = col;
+    col += kOutCols;
+  }
+  uint32_t alloc = 32;
+  while (alloc < col) alloc <<= 1;
+  L.tmem_cols = alloc;
+  return L;
 }
+
+struct FusedParams {
+  NetDims nd;
+  Layout lay;
+  const float *pos;
+  const float *tgt;
+  const float *dext;
+  float *out;
+  const float *table32;
+  const __half *table16;
+  const uint8_t *wimage;
+  float *gm;
+  int32_t *gh_fixed;
+  float *gh_float;
+  uint8_t *touched;
+  double *loss_acc;
+  int *err;
+  float inv_N;
+  float dscale;      // dY scale (power of two)
+  float inv_dscale;
+  uint32_t N;
+  uint32_t ntiles;
+  int mode;          // 0 internal loss, 1 external dL/dy
+};
+
+// ------------------------------------------------------------- device parts
+
+template <int D>
+struct Cell {
+  int32_t bc[D];
+  float frac[D];
+};
+
+template <int D>
+__device__ __forceinline__ void cell_of(const float *p, float res, Cell<D> &c) {
+#pragma unroll
+  for (int a = 0; a < D; ++a) {
+    const float s = __fmul_rn(p[a], res);
+    const float fl = floorf(s);
+    c.bc[a] = (int32_t)fl;
+    c.frac[a] = __fsub_rn(s, fl);
+  }
+}
+
+// corner k (dx fastest, then dy, dz, dw): table element offset of feature 0
+// and the weight product ((wx*wy)*wz)*wt.
+template <int D, int F>
+__device__ __forceinline__ void corner(const Cell<D> &c, int k, uint32_t mask,
+                                       uint64_t level_base, uint32_t &off,
+                                       float &w) {
+  const int dx = k & 1, dy = (k >> 1) & 1, dz = (k >> 2) & 1, dw = (k >> 3) & 1;
+  uint32_t h;
+  if (D == 4)
+    h = hash4(c.bc[0] + dx, c.bc[1] + dy, c.bc[2] + dz, c.bc[D - 1] + dw, mask);
+  else
+    h = hash3(c.bc[0] + dx, c.bc[1] + dy, c.bc[2] + dz, mask);
+  off = (uint32_t)(level_base + (uint64_t)h * F);
+  const float wx = dx ? c.frac[0] : 1.0f - c.frac[0];
+  const float wy = dy ? c.frac[1] : 1.0f - c.frac[1];
+  const float wz = dz ? c.frac[2] : 1.0f - c.frac[2];
+  w = __fmul_rn(__fmul_rn(wx, wy), wz);
+  if (D == 4) {
+    const float wt = dw ? c.frac[D - 1] : 1.0f - c.frac[D - 1];
+    w = __fmul_rn(w, wt);
+  }
+}
+
+template <int F, bool HALF>
+__device__ __forceinline__ void load_entry(const FusedParams &P, uint32_t off,
+                                           float *v) {
+  if (HALF) {
+    const __half *t = P.table16 + off;
+    if (F == 1) {
+      v[0] = __half2float(__ldg(t));
+    } else if (F == 2) {
+      const __half2 h = __ldg(reinterpret_cast<const __half2 *>(t));
+      v[0] = __low2float(h);
+      v[1] = __high2float(h);
+    } else {
+      const uint2 u = __ldg(reinterpret_cast<const uint2 *>(t));
+      const __half2 a = *reinterpret_cast<const __half2 *>(&u.x);
+      const __half2 b = *reinterpret_cast<const __half2 *>(&u.y);
+      v[0] = __low2float(a);
+      v[1] = __high2float(a);
+      v[2] = __low2float(b);
+      v[3] = __high2float(b);
+    }
+  } else {
+    const float *t = P.table32 + off;
+    if (F == 1) {
+      v[0] = __ldg(t);
+    } else if (F == 2) {
+      const float2 f = __ldg(reinterpret_cast<const float2 *>(t));
+      v[0] = f.x;
+      v[1] = f.y;
+    } else {
+      const float4 f = __ldg(reinterpret_cast<const float4 *>(t));
+      v[0] = f.x;
+      v[1] = f.y;
+      v[2] = f.z;
+      v[3] = f.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void red_add_f32x2(float *addr, float a, float b) {
+  asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr),
+               "f"(a), "f"(b)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_f32x4(float *addr, float a, float b,
+                                              float c, float d) {
+  asm volatile(
+      "red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr),
+      "f"(a), "f"(b), "f"(c), "f"(d)
+      : "memory");
+}
+
+// Point loss and dL/dy (reference order, fp32).
+__device__ __forceinline__ float loss_and_grad(const NetDims &nd, const float *y,
+                                               const float *t, float inv_N,
+                                               float *d) {
+  const int O = nd.O;
+  if (nd.loss == 3) {
+    float dot = 0.f, pn = 0.f, tn = 0.f;
+    for (int m = 0; m < O; ++m) {
+      dot += y[m] * t[m];
+      pn += y[m] * y[m];
+      tn += t[m] * t[m];
+    }
+    const float pred_norm = sqrtf(pn + 1e-8f), target_norm = sqrtf(tn + 1e-8f);
+    const float denom = pred_norm * target_norm, cosine = dot / denom;
+    for (int m = 0; m < O; ++m)
+      d[m] = ((cosine * y[m]) / (pn + 1e-8f) - t[m] / denom) * inv_N;
+    return 1.0f - cosine;
+  }
+  float loss = 0.f;
+  for (int m = 0; m < O; ++m) {
+    const float r = y[m] - t[m];
+    if (nd.loss == 0) {
+      loss += r * r;
+      d[m] = (2.0f * r) * inv_N;
+    } else if (nd.loss == 1) {
+      loss += fabsf(r);
+      d[m] = (r > 0.f ? 1.f : (r < 0.f ? -1.f : 0.f)) * inv_N;
+    } else {
+      const float ar = fabsf(r), delta = nd.huber_delta;
+      if (ar <= delta) {
+        loss += (0.5f * r) * r;
+        d[m] = r * inv_N;
+      } else {
+        loss += delta * (ar - 0.5f * delta);
+        d[m] = (delta * (r > 0.f ? 1.f : -1.f)) * inv_N;
+      }
+    }
+  }
+  return loss;
+}
+
+// Writes 16 fp32 values as fp16 into row r, columns c0..c0+15 of a
+// core-blocked tile (two 16-byte stores).
+__device__ __forceinline__ void store_row16(__half *tile, int cols, int r,
+                                            int c0, const float *v) {
+  uint4 u[2];
+  __half2 *h = reinterpret_cast<__half2 *>(u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4 *>(tile + tc::cb(r, c0, cols)) = u[0];
+  *reinterpret_cast<uint4 *>(tile + tc::cb(r, c0 + 8, cols)) = u[1];
+}
+
+__device__ __forceinline__ void load_row16(const __half *tile, int cols, int r,
+                                           int c0, float *v) {
+  uint4 u[2];
+  u[0] = *reinterpret_cast<const uint4 *>(tile + tc::cb(r, c0, cols));
+  u[1] = *reinterpret_cast<const uint4 *>(tile + tc::cb(r, c0 + 8, cols));
+  const __half2 *h = reinterpret_cast<const __half2 *>(u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <int D, int F, int W, bool HALF, bool TRAIN>
+__global__ void __launch_bounds__(kThreads)
+    k_fused(const __grid_constant__ FusedParams P) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const NetDims &nd = P.nd;
+  const Layout &Ly = P.lay;
+  const int t = threadIdx.x;
+  const int warp = t >> 5;
+  const int In = nd.In, H = nd.H, O = nd.O;
+  uint64_t *mbar = reinterpret_cast<uint64_t *>(sm + Ly.misc);
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + Ly.misc + 8);
+  float *s_red = reinterpret_cast<float *>(sm + Ly.misc + 64);  // 16 + 4
+  __half *X = reinterpret_cast<__half *>(sm + Ly.x);
+
+  // ---- prologue: weights to shared, ones columns, barrier, TMEM
+  {
+    const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage);
+    uint4 *dst = reinterpret_cast<uint4 *>(sm);
+    for (uint32_t i = t; i < Ly.image_bytes / 16; i += kThreads) dst[i] = src[i];
+    if (TRAIN) {
+      float ones[16] = {1.f};
+      store_row16(X, Ly.xc, t, In, ones);
+      for (int k = 0; k < H; ++k)
+        store_row16(reinterpret_cast<__half *>(sm + Ly.h[k]), Ly.hc, t, W, ones);
+    }
+    if (t < 20) s_red[t] = 0.f;
+    if (t == 0) tc::mbar_init(tc::smem_u32(mbar), 1);
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(tslot), Ly.tmem_cols);
+  }
+  tc::fence_proxy_async();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t T_s = tmem + Ly.t_scratch;
+  const float *bias0 = reinterpret_cast<const float *>(sm + Ly.b[0]);
+  const uint32_t mbar_a = tc::smem_u32(mbar);
+  const uint32_t sbase = tc::smem_u32(sm);
+  uint32_t phase = 0;
+  bool ok = true;
+  bool first = true;
+  float loss_sum = 0.f;
+  float db_out[kOutCols];
+#pragma unroll
+  for (int m = 0; m < kOutCols; ++m) db_out[m] = 0.f;
+  const uint32_t tmask = nd.T - 1u;
+
+  auto sync_mma = [&]() {
+    // called by every thread after thread 0 committed
+    if (!tc::mbar_wait(mbar_a, phase, kWaitBound)) {
+      ok = false;
+      if (t == 0) atomicExch(P.err, 1);
+    }
+    phase ^= 1u;
+    tc::fence_after_sync();
+  };
+  auto publish = [&]() {
+    // shared writes visible to the tensor core; TMEM reads retired
+    tc::fence_proxy_async();
+    tc::fence_before_sync();
+    __syncthreads();
+  };
+
+  for (uint32_t tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
+    const uint32_t row = tile * kTile + t;
+    const bool valid = row < P.N;
+    float p[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+#pragma unroll
+      for (int a = 0; a < D; ++a) p[a] = __ldg(P.pos + (size_t)row * D + a);
+    }
+    // ---- encode
+    {
+      float acc[16];
+      int filled = 0;
+      for (int l = 0; l < nd.L; ++l) {
+        Cell<D> c;
+        cell_of<D>(p, nd.res[l], c);
+        const uint64_t lb = (uint64_t)l * nd.T * F;
+        float f[F];
+#pragma unroll
+        for (int q = 0; q < F; ++q) f[q] = 0.f;
+        uint32_t offs[1 << D];
+        float ws[1 << D];
+#pragma unroll
+        for (int k = 0; k < (1 << D); ++k) corner<D, F>(c, k, tmask, lb, offs[k], ws[k]);
+        float vals[1 << D][F];
+#pragma unroll
+        for (int k = 0; k < (1 << D); ++k) load_entry<F, HALF>(P, offs[k], vals[k]);
+#pragma unroll
+        for (int k = 0; k < (1 << D); ++k)
+#pragma unroll
+          for (int q = 0; q < F; ++q) f[q] = __fadd_rn(f[q], __fmul_rn(ws[k], vals[k][q]));
+#pragma unroll
+        for (int q = 0; q < F; ++q) acc[filled + q] = f[q];
+        filled += F;
+        if (filled == 16) {
+          store_row16(X, Ly.xc, t, l * F + F - 16, acc);
+          filled = 0;
+        }
+      }
+    }
+    publish();
+    // ---- forward
+    const int nh_tiles = Ly.n_h_tiles;
+    for (int k = 0; k < H; ++k) {
+      const int hk = TRAIN ? k : (k & 1);
+      const int hp = TRAIN ? k - 1 : ((k - 1) & 1);
+      if (t == 0) {
+        tc::fence_after_sync();
+        tc::Operand A = k == 0 ? tc::Operand{sbase + Ly.x, Ly.xc, 0}
+                               : tc::Operand{sbase + Ly.h[hp], Ly.hc, 0};
+        tc::Operand B{sbase + Ly.w[k], W, 1};
+        tc::gemm(T_s, A, B, kTile, W, k == 0 ? In : W, 0);
+        tc::commit(mbar_a);
+      }
+      sync_mma();
+      if (!ok) break;
+      const float *bk = reinterpret_cast<const float *>(sm + Ly.b[k]);
+      __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[hk]);
+#pragma unroll
+      for (int c0 = 0; c0 < W; c0 += 16) {
+        float v[16];
+        tc::tmem_ld16(T_s + lane_base + c0, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i] + bk[c0 + i], 0.f);
+        store_row16(Hk, Ly.hc, t, c0, v);
+      }
+      publish();
+    }
+    (void)nh_tiles;
+    (void)bias0;
+    if (!ok) break;
+    const int hl = TRAIN ? H - 1 : ((H - 1) & 1);
+    // ---- output layer
+    if (t == 0) {
+      tc::fence_after_sync();
+      tc::gemm(T_s, tc::Operand{sbase + Ly.h[hl], Ly.hc, 0},
+               tc::Operand{sbase + Ly.w[H], kOutCols, 1}, kTile, kOutCols, W, 0);
+      tc::commit(mbar_a);
+    }
+    sync_mma();
+    if (!ok) break;
+    float y[kOutCols];
+    tc::tmem_ld16(T_s + lane_base, y);
+    const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
+#pragma unroll
+    for (int m = 0; m < kOutCols; ++m) y[m] += bo[m];
+    if (!TRAIN) {
+      if (valid)
+        for (int m = 0; m < O; ++m) P.out[(size_t)row * O + m] = y[m];
+      tc::fence_before_sync();
+      __syncthreads();
+      continue;
+    }
+    // ---- loss / external gradient -> dY (scaled) in shared memory
+    {
+      float d[kOutCols];
+#pragma unroll
+      for (int m = 0; m < kOutCols; ++m) d[m] = 0.f;
+      if (valid) {
+        if (P.mode == 0) {
+          float tg[kOutCols];
+          for (int m = 0; m < O; ++m) tg[m] = __ldg(P.tgt + (size_t)row * O + m);
+          loss_sum += loss_and_grad(nd, y, tg, P.inv_N, d);
+        } else {
+          for (int m = 0; m < O; ++m) d[m] = __ldg(P.dext + (size_t)row * O + m);
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kOutCols; ++m) {
+        db_out[m] += d[m];
+        d[m] *= P.dscale;
+      }
+      store_row16(reinterpret_cast<__half *>(sm + Ly.dy), kOutCols, t, 0, d);
+    }
+    publish();
+    // ---- backward through the output layer
+    int cur = 0;
+    if (t == 0) {
+      tc::fence_after_sync();
+      // dH = dY . Wout^T   (B = Wout stored [W x 16] as K-major rows N = j)
+      tc::gemm(T_s, tc::Operand{sbase + Ly.dy, kOutCols, 0},
+               tc::Operand{sbase + Ly.w[H], kOutCols, 0}, kTile, W, kOutCols, 0);
+      // dWout += H^T . dY
+      tc::gemm(tmem + Ly.t_dwout, tc::Operand{sbase + Ly.h[hl], Ly.hc, 1},
+               tc::Operand{sbase + Ly.dy, kOutCols, 1}, W, kOutCols, kTile,
+               first ? 0u : 1u);
+      tc::commit(mbar_a);
+    }
+    sync_mma();
+    if (!ok) break;
+    for (int k = H - 1; k >= 0; --k) {
+      // dpre_k = D * relu'(H_k) -> dH[cur]
+      {
+        const __half *Hk = reinterpret_cast<const __half *>(sm + Ly.h[k]);
+        __half *dHt = reinterpret_cast<__half *>(sm + Ly.dh[cur]);
+#pragma unroll
+        for (int c0 = 0; c0 < W; c0 += 16) {
+          float v[16], hv[16];
+          tc::tmem_ld16(T_s + lane_base + c0, v);
+          load_row16(Hk, Ly.hc, t, c0, hv);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = hv[i] > 0.f ? v[i] : 0.f;
+          store_row16(dHt, W, t, c0, v);
+        }
+      }
+      publish();
+      if (t == 0) {
+        tc::fence_after_sync();
+        const tc::Operand dHk{sbase + Ly.dh[cur], W, 0};
+        const tc::Operand dHkT{sbase + Ly.dh[cur], W, 1};
+        if (k > 0) {
+          // D = dH_k . W_k^T  (B = W_k stored [W x W] K-major rows N = i)
+          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[k], W, 0}, kTile, W, W, 0);
+          // dW_k^T += dH_k^T . [H_(k-1) | 1]
+          tc::gemm(tmem + Ly.t_dwk[k], dHkT,
+                   tc::Operand{sbase + Ly.h[k - 1], Ly.hc, 1}, W, W + 16, kTile,
+                   first ? 0u : 1u);
+        } else {
+          // dX = dH_0 . W0^T  (B = W0 stored [In x W] K-major rows N = i)
+          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[0], W, 0}, kTile, In, W, 0);
+          // dW0^T += dH_0^T . [X | 1]
+          tc::gemm(tmem + Ly.t_dw0, dHkT, tc::Operand{sbase + Ly.x, Ly.xc, 1}, W,
+                   In + 16, kTile, first ? 0u : 1u);
+        }
+        tc::commit(mbar_a);
+      }
+      sync_mma();
+      if (!ok) break;
+      cur ^= 1;
+    }
+    if (!ok) break;
+    first = false;
+    // ---- scatter d_feature * corner weight into the hash gradients
+    {
+      const int levels = nd.active_levels;
+      for (int l0 = 0; l0 < levels; l0 += 16 / F) {
+        float df[16];
+        tc::tmem_ld16(T_s + lane_base + l0 * F, df);
+        if (!valid) continue;
+        const int lend = min(levels, l0 + 16 / F);
+        for (int l = l0; l < lend; ++l) {
+          float dfe[F];
+#pragma unroll
+          for (int q = 0; q < F; ++q) dfe[q] = df[(l - l0) * F + q] * P.inv_dscale;
+          Cell<D> c;
+          cell_of<D>(p, nd.res[l], c);
+          const uint64_t lb = (uint64_t)l * nd.T * F;
+#pragma unroll
+          for (int k = 0; k < (1 << D); ++k) {
+            uint32_t off;
+            float w;
+            corner<D, F>(c, k, tmask, lb, off, w);
+            if (nd.grad_fixed) {
+#pragma unroll
+              for (int q = 0; q < F; ++q)
+                atomicAdd(P.gh_fixed + off + q,
+                          fixed_trunc(__fmul_rn(__fmul_rn(dfe[q], w), kGradScale)));
+            } else if (F == 2) {
+              red_add_f32x2(P.gh_float + off, dfe[0] * w, dfe[F - 1] * w);
+            } else if (F == 4) {
+              red_add_f32x4(P.gh_float + off, dfe[0] * w, dfe[1 % F] * w,
+                            dfe[2 % F] * w, dfe[3 % F] * w);
+            } else {
+              atomicAdd(P.gh_float + off, dfe[0] * w);
+            }
+            if (F == 2)
+              P.touched[off >> 1] = 1;
+            else if (F == 4)
+              *reinterpret_cast<uint32_t *>(P.touched + off) = 0x01010101u;
+            else
+              P.touched[off] = 1;
+          }
+        }
+      }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+  }
+
+  // ---- epilogue: weight gradients, bias of the output layer, loss
+  if (TRAIN && !first && ok) {
+    tc::fence_after_sync();
+    // M = W: row r of an accumulator lives in lane r (W == 128) or in lane
+    // (r / 16) * 32 + r % 16 (W == 64).
+    const int lane = t & 31;
+    const bool has_row = W == 128 || lane < 16;
+    const int r = W == 128 ? t : warp * 16 + lane;
+    const float s = P.inv_dscale;
+    auto flush = [&](uint32_t tcol, int ncols, auto &&dest) {
+      for (int c0 = 0; c0 < ncols; c0 += 16) {
+        float v[16];
+        tc::tmem_ld16(tmem + lane_base + tcol + c0, v);
+        if (!has_row) continue;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = c0 + i;
+          float *dst = dest(c);
+          if (dst && v[i] != 0.f) atomicAdd(dst, v[i] * s);
+        }
+      }
+    };
+    // dW0^T[j][i] -> W0[i][j]; column In is the bias gradient of layer 0
+    flush(Ly.t_dw0, In + 16, [&](int c) -> float * {
+      if (c < In) return P.gm + nd.w_off[0] + (int64_t)c * W + r;
+      if (c == In) return P.gm + nd.b_off[0] + r;
+      return nullptr;
+    });
+    for (int k = 1; k < H; ++k)
+      flush(Ly.t_dwk[k], W + 16, [&](int c) -> float * {
+        if (c < W) return P.gm + nd.w_off[k] + (int64_t)c * W + r;
+        if (c == W) return P.gm + nd.b_off[k] + r;
+        return nullptr;
+      });
+    flush(Ly.t_dwout, kOutCols, [&](int c) -> float * {
+      return c < O ? P.gm + nd.w_off[H] + (int64_t)r * O + c : nullptr;
+    });
+  }
+  if (TRAIN) {
+    // output bias gradient and loss: warp reduction, then shared, then global
+#pragma unroll
+    for (int m = 0; m < kOutCols; ++m) {
+      float v = db_out[m];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if ((t & 31) == 0 && m < O) atomicAdd(s_red + m, v);
+    }
+    float ls = loss_sum;
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if ((t & 31) == 0) atomicAdd(s_red + 16, ls);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (TRAIN && t == 0) {
+    for (int m = 0; m < O; ++m)
+      if (s_red[m] != 0.f) atomicAdd(P.gm + nd.b_off[H] + m, s_red[m]);
+    if (P.mode == 0) atomicAdd(P.loss_acc, (double)s_red[16]);
+  }
+  if (warp == 0) tc::tmem_dealloc(tmem, Ly.tmem_cols);
+}
+
+// Packs the fp32 MLP weights into the fp16 core-blocked image.
+__global__ void k_pack(NetDims nd, Layout Ly, const float *__restrict__ mlp,
+                       uint8_t *img) {
+  const int W = nd.W, In = nd.In, H = nd.H, O = nd.O;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  // W0 [In x W]
+  if (i < In * W) {
+    const int r = i / W, c = i % W;
+    reinterpret_cast<__half *>(img + Ly.w[0])[tc::cb(r, c, W)] =
+        __float2half_rn(mlp[nd.w_off[0] + i]);
+  }
+  for (int k = 1; k < H; ++k)
+    if (i < W * W) {
+      const int r = i / W, c = i % W;
+      reinterpret_cast<__half *>(img + Ly.w[k])[tc::cb(r, c, W)] =
+          __float2half_rn(mlp[nd.w_off[k] + i]);
+    }
+  if (i < W * kOutCols) {
+    const int r = i / kOutCols, c = i % kOutCols;
+    reinterpret_cast<__half *>(img + Ly.w[H])[tc::cb(r, c, kOutCols)] =
+        __float2half_rn(c < O ? mlp[nd.w_off[H] + (int64_t)r * O + c] : 0.f);
+  }
+  for (int k = 0; k < H; ++k)
+    if (i < W) reinterpret_cast<float *>(img + Ly.b[k])[i] = mlp[nd.b_off[k] + i];
+  if (i < kOutCols)
+    reinterpret_cast<float *>(img + Ly.b[H])[i] = i < O ? mlp[nd.b_off[H] + i] : 0.f;
+}
+
+using KernelFn = void (*)(FusedParams);
+
+template <int D, int F, bool HALF, bool TRAIN>
+KernelFn pick_w(int W) {
+  switch (W) {
+    case 16: return TRAIN ? nullptr : (KernelFn)k_fused<D, F, 16, HALF, TRAIN>;
+    case 32: return TRAIN ? nullptr : (KernelFn)k_fused<D, F, 32, HALF, TRAIN>;
+    case 64: return (KernelFn)k_fused<D, F, 64, HALF, TRAIN>;
+    case 128: return (KernelFn)k_fused<D, F, 128, HALF, TRAIN>;
+  }
+  return nullptr;
+}
+
+template <bool TRAIN>
+KernelFn pick(int d, int F, int W, bool half) {
+#define TMNN_PICK(DD, FF)                                                       \
+  if (d == DD && F == FF)                                                       \
+    return half ? pick_w<DD, FF, true, TRAIN>(W) : pick_w<DD, FF, false, TRAIN>(W);
+  TMNN_PICK(3, 1) TMNN_PICK(3, 2) TMNN_PICK(3, 4)
+  TMNN_PICK(4, 1) TMNN_PICK(4, 2) TMNN_PICK(4, 4)
+#undef TMNN_PICK
+  return nullptr;
+}
+
+bool shape_ok(const NetDims &nd, bool train, std::string *why) {
+  auto no = [&](const char *m) {
+    if (why) *why = m;
+    return false;
+  };
+  if (nd.In % 16 != 0 || nd.In > 128)
+    return no("encoding width (levels x features) must be a multiple of 16, <= 128");
+  if (nd.O > kOutCols) return no("more than 16 outputs");
+  if (train) {
+    if (nd.W != 64 && nd.W != 128) return no("hidden width must be 64 or 128");
+    if (nd.H > kMaxTrainHidden) return no("more than 4 hidden layers");
+  } else if (nd.W % 16 != 0 || nd.W > 128) {
+    return no("hidden width must be 16, 32, 64 or 128");
+  }
+  const Layout L = make_layout(nd, train);
+  if (L.total > 200 * 1024) return no("shared memory tile exceeds 200 KB");
+  if (L.tmem_cols > 512) return no("TMEM columns exceed 512");
+  return true;
+}
+
+NetDims dims_of(const tmnn_spec &s) {
+  NetDims nd{};
+  nd.L = s.n_levels;
+  nd.F = s.n_features_per_level;
+  nd.d = s.spatial_dims;
+  nd.W = s.hidden_dim;
+  nd.H = s.num_hidden_layers;
+  nd.O = s.num_outputs;
+  nd.In = nd.L * nd.F;
+  return nd;
+}
+
+int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+           const float *params, const __half *table_h, bool train,
+           FusedParams &P, int num_sms, cudaStream_t st) {
+  const Layout Ly = make_layout(nd, train);
+  int launches = 0;
+  if (!ws.err) {
+    if (cudaMalloc(&ws.err, sizeof(int)) != cudaSuccess)
+      throw std::runtime_error("fused: cudaMalloc failed");
+    cudaMemsetAsync(ws.err, 0, sizeof(int), st);
+  }
+  // (re)pack the weight images when the weights changed
+  if (ws.dirty || ws.wpack_bytes < 2ull * Ly.image_bytes) {
+    const Layout Lt = make_layout(nd, true), Lf = make_layout(nd, false);
+    const size_t need = (size_t)Lt.image_bytes + Lf.image_bytes;
+    if (ws.wpack_bytes < need) {
+      if (ws.wpack) cudaFree(ws.wpack);
+      if (cudaMalloc(&ws.wpack, need) != cudaSuccess)
+        throw std::runtime_error("fused: cudaMalloc failed");
+      ws.wpack_bytes = need;
+    }
+    cudaMemsetAsync(ws.wpack, 0, need, st);
+    const float *mlp = params + nd.hash_count;
+    const int n = nd.W * nd.W > nd.In * nd.W ? nd.W * nd.W : nd.In * nd.W;
+    const int grid = (n + 255) / 256 + 1;
+    k_pack<<<grid, 256, 0, st>>>(nd, Lt, mlp, (uint8_t *)ws.wpack);
+    k_pack<<<grid, 256, 0, st>>>(nd, Lf, mlp,
+                                 (uint8_t *)ws.wpack + Lt.image_bytes);
+    launches += 2;
+    ws.dirty = false;
+  }
+  P.nd = nd;
+  P.lay = Ly;
+  P.wimage = (const uint8_t *)ws.wpack +
+             (train ? 0 : make_layout(nd, true).image_bytes);
+  P.table32 = params;
+  P.table16 = table_h;
+  P.err = ws.err;
+  P.ntiles = (P.N + kTile - 1) / kTile;
+  const bool half = spec.table_dtype == TMNN_DTYPE_F16 && table_h;
+  KernelFn fn = train ? pick<true>(nd.d, nd.F, nd.W, half)
+                      : pick<false>(nd.d, nd.F, nd.W, half);
+  if (!fn) throw std::runtime_error("fused: no kernel for this shape");
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)Ly.total);
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, Ly.total);
+  const int tmem_fit = (int)(512 / Ly.tmem_cols);
+  if (per_sm > tmem_fit) per_sm = tmem_fit;
+  if (per_sm < 1) per_sm = 1;
+  ws.ctas_per_sm = per_sm;
+  uint32_t grid = (uint32_t)num_sms * per_sm;
+  if (grid > P.ntiles) grid = P.ntiles;
+  if (grid == 0) return launches;
+  fn<<<grid, kThreads, Ly.total, st>>>(P);
+  return launches + 1;
+}
+
+}  // namespace
+
+bool fused_supported(const tmnn_spec &spec, const tmnn_train_cfg &cfg,
+                     std::string *why) {
+  (void)cfg;
+  NetDims nd = dims_of(spec);
+  return shape_ok(nd, true, why) && shape_ok(nd, false, why);
+}
+
 void fused_weights_changed(FusedWorkspace &ws) { ws.dirty = true; }
+
 void fused_release(FusedWorkspace &ws) {
   if (ws.wpack) cudaFree(ws.wpack);
+  if (ws.err) cudaFree(ws.err);
   ws.wpack = nullptr;
+  ws.err = nullptr;
+  ws.wpack_bytes = 0;
 }
-int fused_train(FusedWorkspace &, const NetDims &, const tmnn_spec &,
-                const float *, const __half *, const float *, const float *,
-                const float *, float, float *, int32_t *, float *, uint8_t *,
-                double *, uint32_t, int, cudaStream_t) {
-  return 0;
+
+int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+                const float *params, const __half *table_h, const float *pos,
+                const float *tgt, const float *dext, float inv_N, float *gm,
+                int32_t *gh_fixed, float *gh_float, uint8_t *touched,
+                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st) {
+  FusedParams P{};
+  P.pos = pos;
+  P.tgt = tgt;
+  P.dext = dext;
+  P.gm = gm;
+  P.gh_fixed = gh_fixed;
+  P.gh_float = gh_float;
+  P.touched = touched;
+  P.loss_acc = loss_acc;
+  P.inv_N = inv_N;
+  // dY scale: a power of two near 1/inv_N (the batch), so fp16 dY ~ O(1)
+  int e = 0;
+  if (dext) {
+    P.dscale = 1.0f;
+  } else {
+    frexpf(inv_N > 0.f ? 1.0f / inv_N : 1.0f, &e);
+    P.dscale = ldexpf(1.0f, e - 1);
+  }
+  P.inv_dscale = 1.0f / P.dscale;
+  P.N = N;
+  P.mode = dext ? 1 : 0;
+  return launch(ws, nd, spec, params, table_h, true, P, num_sms, st);
 }
-int fused_forward(FusedWorkspace &, const NetDims &, const tmnn_spec &,
-                  const float *, const __half *, const float *, float *,
-                  uint32_t, int, cudaStream_t) {
-  return 0;
+
+int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+                  const float *params, const __half *table_h, const float *pos,
+                  float *out, uint32_t N, int num_sms, cudaStream_t st) {
+  FusedParams P{};
+  P.pos = pos;
+  P.out = out;
+  P.N = N;
+  P.dscale = P.inv_dscale = 1.0f;
+  return launch(ws, nd, spec, params, table_h, false, P, num_sms, st);
+}
+
+int fused_error(FusedWorkspace &ws, cudaStream_t st) {
+  if (!ws.err) return 0;
+  int h = 0;
+  cudaMemcpyAsync(&h, ws.err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  cudaStreamSynchronize(st);
+  return h;
 }
 
 }  // namespace tmnn

@@ -13,13 +13,15 @@
 
 namespace tmnn {
 
-// Device-side packed weights (fp16, tensor-core layouts), rebuilt lazily
-// after every weight change.
+// Device-side state of the family: the fp16 weight image (rebuilt lazily
+// after every weight change) and an error word the kernels set when a
+// bounded wait on the tensor-core pipeline gives up.
 struct FusedWorkspace {
   void *wpack = nullptr;
   size_t wpack_bytes = 0;
   bool dirty = true;
   int ctas_per_sm = 0;
+  int *err = nullptr;
 };
 
 bool fused_supported(const tmnn_spec &spec, const tmnn_train_cfg &cfg,
@@ -35,5 +37,7 @@ int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
 int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                   const float *params, const __half *table_h, const float *pos,
                   float *out, uint32_t N, int num_sms, cudaStream_t st);
+// Nonzero when a fused kernel reported a timed-out pipeline wait.
+int fused_error(FusedWorkspace &ws, cudaStream_t st);
 
 }  // namespace tmnn
