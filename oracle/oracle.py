@@ -25,7 +25,8 @@ class Spec(C.Structure):
                 ("O", C.c_int32), ("loss", C.c_int32), ("base", C.c_float),
                 ("scale", C.c_float), ("huber_delta", C.c_float),
                 ("active_levels", C.c_int32), ("grad_mode", C.c_int32),
-                ("res_mode", C.c_int32)]
+                ("res_mode", C.c_int32), ("fp16_operands", C.c_int32),
+                ("dscale", C.c_float)]
 
 
 class AdamCfg(C.Structure):
@@ -100,10 +101,17 @@ def _p(a):
 
 def make_spec(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss="L2",
               base=16.0, scale=1.447, huber_delta=1.0, active_levels=0,
-              grad_mode=GRAD_FIXED16, res_mode=0):
+              grad_mode=GRAD_FIXED16, res_mode=0, fp16_operands=0, dscale=0.0):
     return Spec(L, F, log2T, d, W, H, O, LOSS[loss] if isinstance(loss, str)
                 else loss, base, scale, huber_delta, active_levels, grad_mode,
-                res_mode)
+                res_mode, fp16_operands, dscale)
+
+
+def pow2_scale(n):
+    """The fused kernel's dL/dy scale for a batch of n: 2^(e-1) where
+    n = m * 2^e with m in [0.5, 1) (frexp)."""
+    import math
+    return math.ldexp(1.0, math.frexp(float(max(n, 1)))[1] - 1)
 
 
 def hash_grid_size(s):
@@ -288,6 +296,8 @@ class OracleTrainer:
         adam(self.s, self.w, self.m, self.v, g, self.step,
              nthreads=self.nthreads, **self.opt)
         self.step += 1
+        if pos.shape[0] == 0:
+            return 0.0
         return float(np.float32(loss) / np.float32(pos.shape[0]))
 
     def evaluate(self, pos):

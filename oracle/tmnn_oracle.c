@@ -214,36 +214,41 @@ static void mlp_offsets(const tmo_spec *s, offsets_t *o) {
 /* Encode fused with W0 (mlp_kernel_emitter.cpp:279-296 float2 path:
  * h0[j] += f.x*W0[2l][j] + f.y*W0[2l+1][j]; scalar path :343-358:
  * h0[j] += feat*W0[row][j]); then h0 = max(h0 + b0, 0) (:2950-2951). */
+/* fp16 operand rounding of the tensor-core emulation mode (identity
+ * otherwise). */
+static inline float r16(int on, float x) { return on ? (float)(_Float16)x : x; }
+
 static void forward_point(const tmo_spec *s, const float *res,
                           const float *table, const float *mlp,
                           const offsets_t *o, const float *p,
                           float acts[MAX_H][MAX_W], float *y) {
-  const int W = s->W;
+  const int W = s->W, e = s->fp16_operands;
   float *h0 = acts[0];
   for (int j = 0; j < W; ++j) h0[j] = 0.0f;
   const int vec2 = (s->F == 2 && s->d == 3);
   for (int l = 0; l < s->L; ++l) {
     corners_t c;
-    float feat[4];
+    float feat[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     level_corners(s, p, res[l], l, &c);
     level_features(s, table, &c, feat);
+    for (int f = 0; f < s->F; ++f) feat[f] = r16(e, feat[f]);
     if (vec2) {
       const float *wa = mlp + o->w_off[0] + (int64_t)(2 * l) * W;
       const float *wb = wa + W;
       for (int j = 0; j < W; ++j) {
-        const float t = feat[0] * wa[j] + feat[1] * wb[j];
+        const float t = feat[0] * r16(e, wa[j]) + feat[1] * r16(e, wb[j]);
         h0[j] = h0[j] + t;
       }
     } else {
       for (int f = 0; f < s->F; ++f) {
         const float *wr = mlp + o->w_off[0] + (int64_t)(l * s->F + f) * W;
-        for (int j = 0; j < W; ++j) h0[j] = h0[j] + feat[f] * wr[j];
+        for (int j = 0; j < W; ++j) h0[j] = h0[j] + feat[f] * r16(e, wr[j]);
       }
     }
   }
   for (int j = 0; j < W; ++j) {
     const float t = h0[j] + mlp[o->b_off[0] + j];
-    h0[j] = t > 0.0f ? t : 0.0f;
+    h0[j] = r16(e, t > 0.0f ? t : 0.0f);
   }
   /* hidden layers (mlp_kernel_emitter.cpp:2962-2970): acc = sum_i h[i]*W[i][j]
    * from 0, then max(acc + b, 0) */
@@ -253,9 +258,10 @@ static void forward_point(const tmo_spec *s, const float *res,
     const float *Wk = mlp + o->w_off[k];
     for (int j = 0; j < W; ++j) {
       float acc = 0.0f;
-      for (int i = 0; i < W; ++i) acc = acc + hin[i] * Wk[(int64_t)i * W + j];
+      for (int i = 0; i < W; ++i)
+        acc = acc + hin[i] * r16(e, Wk[(int64_t)i * W + j]);
       const float t = acc + mlp[o->b_off[k] + j];
-      hout[j] = t > 0.0f ? t : 0.0f;
+      hout[j] = r16(e, t > 0.0f ? t : 0.0f);
     }
   }
   /* output (mlp_kernel_emitter.cpp:2983-2997): acc starts at the bias */
@@ -263,7 +269,8 @@ static void forward_point(const tmo_spec *s, const float *res,
   const float *Wo = mlp + o->w_off[s->H];
   for (int m = 0; m < s->O; ++m) {
     float acc = mlp[o->b_off[s->H] + m];
-    for (int j = 0; j < W; ++j) acc = acc + hl[j] * Wo[(int64_t)j * s->O + m];
+    for (int j = 0; j < W; ++j)
+      acc = acc + hl[j] * r16(e, Wo[(int64_t)j * s->O + m]);
     y[m] = acc;
   }
 }
@@ -374,11 +381,90 @@ static void scatter_one(const tmo_spec *s, scatter_t *sc, uint32_t off,
 
 /* Fused forward + loss + backward + scatter of one point: the scalar train
  * kernel body (mlp_kernel_emitter.cpp:2875-3155). */
+/* The fused tensor-core step with fp16 operands (tmo_spec.fp16_operands):
+ * dL/dy is scaled by dscale and rounded to fp16; every pre-activation
+ * gradient is rounded to fp16 after its ReLU mask; products accumulate in
+ * fp32; weight and table gradients are divided by dscale; the output-bias
+ * gradient uses the unscaled fp32 dL/dy. */
+static float fwd_bwd_point_f16(const tmo_spec *s, const float *res,
+                               const float *table, const float *mlp,
+                               const offsets_t *o, const float *p,
+                               const float *t, const float *dext, float inv_N,
+                               float *gm, scatter_t *sc, float *yout) {
+  const int W = s->W, O = s->O, H = s->H;
+  const float S = s->dscale > 0.0f ? s->dscale : 1.0f, iS = 1.0f / S;
+  float acts[MAX_H][MAX_W], dh[MAX_W], dn[MAX_W];
+  float y[MAX_O], d[MAX_O], ds[MAX_O];
+  forward_point(s, res, table, mlp, o, p, acts, y);
+  if (yout)
+    for (int m = 0; m < O; ++m) yout[m] = y[m];
+  float loss = 0.0f;
+  if (dext) {
+    for (int m = 0; m < O; ++m) d[m] = dext[m];
+  } else {
+    loss = point_loss(s, y, t, inv_N, d);
+  }
+  for (int m = 0; m < O; ++m) ds[m] = r16(1, d[m] * S);
+  const float *hl = acts[H - 1];
+  const float *Wo = mlp + o->w_off[H];
+  for (int j = 0; j < W; ++j) {
+    float acc = 0.0f;
+    for (int m = 0; m < O; ++m) {
+      gm[o->w_off[H] + (int64_t)j * O + m] += (hl[j] * ds[m]) * iS;
+      acc = acc + ds[m] * r16(1, Wo[(int64_t)j * O + m]);
+    }
+    dh[j] = r16(1, hl[j] > 0.0f ? acc : 0.0f);
+  }
+  for (int m = 0; m < O; ++m) gm[o->b_off[H] + m] += d[m];
+  for (int k = H - 1; k >= 1; --k) {
+    const float *hin = acts[k - 1];
+    const float *Wk = mlp + o->w_off[k];
+    for (int i = 0; i < W; ++i) {
+      float acc = 0.0f;
+      for (int j = 0; j < W; ++j) {
+        gm[o->w_off[k] + (int64_t)i * W + j] += (hin[i] * dh[j]) * iS;
+        acc = acc + dh[j] * r16(1, Wk[(int64_t)i * W + j]);
+      }
+      dn[i] = r16(1, hin[i] > 0.0f ? acc : 0.0f);
+    }
+    for (int j = 0; j < W; ++j) gm[o->b_off[k] + j] += dh[j] * iS;
+    for (int i = 0; i < W; ++i) dh[i] = dn[i];
+  }
+  int levels = s->active_levels > 0 ? s->active_levels : s->L;
+  if (levels > s->L) levels = s->L;
+  for (int l = 0; l < levels; ++l) {
+    corners_t c;
+    float feat[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    level_corners(s, p, res[l], l, &c);
+    level_features(s, table, &c, feat);
+    for (int f = 0; f < s->F; ++f) {
+      const int64_t r = o->w_off[0] + (int64_t)(l * s->F + f) * W;
+      const float xf = r16(1, feat[f]);
+      float df = 0.0f;
+      for (int j = 0; j < W; ++j) {
+        gm[r + j] += (xf * dh[j]) * iS;
+        df = df + dh[j] * r16(1, mlp[r + j]);
+      }
+      df = df * iS;
+      for (int k = 0; k < c.n; ++k) {
+        const uint32_t e = c.off[k] + f;
+        scatter_one(s, sc, e, df * c.w[k]);
+        if (sc->touched) sc->touched[s->F == 2 ? e >> 1 : e] = 1;
+      }
+    }
+  }
+  for (int j = 0; j < W; ++j) gm[o->b_off[0] + j] += dh[j] * iS;
+  return loss;
+}
+
 static float fwd_bwd_point(const tmo_spec *s, const float *res,
                            const float *table, const float *mlp,
                            const offsets_t *o, const float *p, const float *t,
                            const float *dext, float inv_N, float *gm,
                            scatter_t *sc, float *yout) {
+  if (s->fp16_operands)
+    return fwd_bwd_point_f16(s, res, table, mlp, o, p, t, dext, inv_N, gm, sc,
+                             yout);
   const int W = s->W, O = s->O, H = s->H;
   float acts[MAX_H][MAX_W];
   float y[MAX_O], d[MAX_O];

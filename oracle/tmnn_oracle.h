@@ -45,6 +45,11 @@ typedef struct tmo_spec {
   int32_t grad_mode;  /* TMO_GRAD_* */
   int32_t res_mode;   /* 0: iterative res*=scale (eval kernel, default);
                          1: base*powf(scale,l) (scalar train kernel) */
+  int32_t fp16_operands; /* 1: round every matrix-product operand to fp16
+                            as a tensor-core kernel consumes it (features,
+                            weights, activations, dL/dy scaled by dscale,
+                            pre-activation gradients); accumulate in fp32 */
+  float dscale;          /* power-of-two dL/dy scale of the fp16 mode */
 } tmo_spec;
 
 /* ---- geometry --------------------------------------------------------- */

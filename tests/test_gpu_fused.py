@@ -51,21 +51,61 @@ def test_fused_forward_matches_oracle(kw):
     tr.close()
 
 
+def emulated_spec(kw, n, grad="F32"):
+    """Oracle spec that rounds matrix operands to fp16 exactly where the
+    tensor-core kernel does, with the kernel's dL/dy scale."""
+    s = oracle_spec(**kw, grad=grad)
+    s.fp16_operands = 1
+    s.dscale = o.pow2_scale(n)
+    return s
+
+
 @pytest.mark.parametrize("kw", CASES)
-def test_fused_gradients_match_oracle(kw):
+def test_fused_gradients_match_fp16_emulating_oracle(kw):
+    """Kernel logic: against the oracle with the same fp16 operand rounding
+    the only differences left are fp32 accumulation order, so the agreement
+    is tight (2e-3)."""
     tr, hw, mw, pos, tgt = setup(kw)
     if kw["loss"] == 3:
         tgt = np.abs(tgt) + 0.1
     lsum = tr.forward_backward(pos, tgt)
-    gh = tr.read_buffer(3)
-    gm = tr.read_buffer(4)
-    touched = tr.read_buffer(21)
-    s = oracle_spec(**kw, grad="F32")
-    lref, g, _ = o.fwd_bwd(s, hw, mw, pos, tgt)
-    assert abs(lsum - lref) <= TOL * abs(lref)
-    assert rel(gh, g["hash_float"]) <= TOL
-    assert rel(gm, g["mlp"]) <= TOL
+    gh, gm, touched = tr.read_buffer(3), tr.read_buffer(4), tr.read_buffer(21)
+    lref, g, _ = o.fwd_bwd(emulated_spec(kw, len(pos)), hw, mw, pos, tgt)
+    assert abs(lsum - lref) <= 1e-3 * abs(lref)
+    assert rel(gh, g["hash_float"]) <= 2e-3
+    assert rel(gm, g["mlp"]) <= 2e-3
     assert np.array_equal(touched, g["touched"])
+    tr.close()
+
+
+@pytest.mark.parametrize("kw", CASES)
+def test_fused_gradients_vs_fp32_oracle(kw):
+    """Precision of fp16 tensor-core math against the fp32 reference math.
+    With default initialisation (hash U(-1e-4, 1e-4), Kaiming MLP) the
+    gradients agree to 1e-2.  With the deliberately large random tables of
+    the stress setup, fp16 activations flip ReLU masks of units whose
+    pre-activation is within fp16 rounding of zero, and each flip moves a
+    whole unit's gradient; the tensor-level error is then ~sqrt(flip rate),
+    a few percent, and is bounded at 5e-2."""
+    tr = cuda_trainer(**kw, family="FullyFused", grad="F32", morton=False)
+    hw, mw = tr.weights()
+    lo = 0.0 if kw.get("d", 3) == 4 else -1.0
+    pos, tgt = batch(4000, kw.get("d", 3), kw["O"], seed=3, lo=lo)
+    if kw["loss"] == 3:
+        tgt = np.abs(tgt) + 0.1
+    lsum = tr.forward_backward(pos, tgt)
+    lref, g, _ = o.fwd_bwd(oracle_spec(**kw, grad="F32"), hw, mw, pos, tgt)
+    assert abs(lsum - lref) <= TOL * abs(lref)
+    assert rel(tr.read_buffer(4), g["mlp"]) <= TOL
+    assert rel(tr.read_buffer(3), g["hash_float"]) <= TOL
+    tr.close()
+    tr, hw, mw, pos, tgt = setup(kw)
+    if kw["loss"] == 3:
+        tgt = np.abs(tgt) + 0.1
+    tr.forward_backward(pos, tgt)
+    _, g, _ = o.fwd_bwd(oracle_spec(**kw, grad="F32"), hw, mw, pos, tgt)
+    assert rel(tr.read_buffer(4), g["mlp"]) <= 5e-2
+    assert rel(tr.read_buffer(3), g["hash_float"]) <= 5e-2
     tr.close()
 
 
@@ -74,10 +114,9 @@ def test_fused_fp16_table_and_fixed_point():
     tr, hw, mw, pos, tgt = setup(kw, table="F16", grad="Fixed16", N=4000)
     tr.forward_backward(pos, tgt)
     gh = tr.read_buffer(3).astype(np.float64)
-    s = oracle_spec(**kw, grad="Fixed16")
     hw16 = hw.astype(np.float16).astype(np.float32)
-    _, g, _ = o.fwd_bwd(s, hw16, mw, pos, tgt)
-    assert rel(gh, g["hash_fixed"].astype(np.float64)) <= 2 * TOL
+    _, g, _ = o.fwd_bwd(emulated_spec(kw, 4000, grad="Fixed16"), hw16, mw, pos, tgt)
+    assert rel(gh, g["hash_fixed"].astype(np.float64)) <= 2e-3
     out = tr.inference(pos)
     ref = o.forward(oracle_spec(**kw), hw16, mw, pos)
     assert np.abs(out - ref).max() <= TOL * np.abs(ref).max()
@@ -89,12 +128,11 @@ def test_fused_ragged_batches(N):
     kw = dict(L=8, F=2, log2T=12, d=3, W=64, H=2, O=2, loss=0)
     tr, hw, mw, pos, tgt = setup(kw, N=N)
     lsum = tr.forward_backward(pos, tgt)
-    s = oracle_spec(**kw, grad="F32")
-    lref, g, _ = o.fwd_bwd(s, hw, mw, pos, tgt)
-    assert abs(lsum - lref) <= TOL * max(abs(lref), 1e-12)
+    lref, g, _ = o.fwd_bwd(emulated_spec(kw, N), hw, mw, pos, tgt)
+    assert abs(lsum - lref) <= 1e-3 * max(abs(lref), 1e-12)
     if N:
-        assert rel(tr.read_buffer(4), g["mlp"]) <= TOL
-        assert rel(tr.read_buffer(3), g["hash_float"]) <= TOL
+        assert rel(tr.read_buffer(4), g["mlp"]) <= 2e-3
+        assert rel(tr.read_buffer(3), g["hash_float"]) <= 2e-3
     out = tr.inference(pos)
     assert out.shape == (N, 2)
     tr.close()
@@ -106,17 +144,16 @@ def test_fused_external_gradient():
     d_out = (np.random.default_rng(5).normal(size=(2000, 3)) * 1e-3).astype(np.float32)
     tr.zero_gradients()
     tr.backward_accumulate(pos, d_out)
-    s = oracle_spec(**kw, grad="F32")
-    _, g, _ = o.fwd_bwd(s, hw, mw, pos, None, d_out=d_out)
-    assert rel(tr.read_buffer(3), g["hash_float"]) <= TOL
-    assert rel(tr.read_buffer(4), g["mlp"]) <= TOL
+    _, g, _ = o.fwd_bwd(emulated_spec(kw, 2000), hw, mw, pos, None, d_out=d_out)
+    assert rel(tr.read_buffer(3), g["hash_float"]) <= 2e-3
+    assert rel(tr.read_buffer(4), g["mlp"]) <= 2e-3
     tr.close()
 
 
 def test_fused_loss_curve_within_2_percent():
     """1000 steps of the SDF-shaped problem: the fused CUDA trainer and the
     CPU oracle trainer, same seeds and batches; loss curves agree to 2 %
-    (averaged over the last 50 steps)."""
+    (averaged over the last 200 steps)."""
     kw = dict(L=8, F=2, log2T=14, d=3, W=64, H=1, O=1, loss=1)
     tr = cuda_trainer(**kw, family="FullyFused", grad="F32", lr_enc=1e-2,
                       lr_net=1e-2)
@@ -128,12 +165,12 @@ def test_fused_loss_curve_within_2_percent():
     radii = rng.uniform(0.1, 0.4, 8).astype(np.float32)
     la, lb = [], []
     for s in range(1000):
-        pos = rng.uniform(-1, 1, (2048, 3)).astype(np.float32)
+        pos = rng.uniform(-1, 1, (4096, 3)).astype(np.float32)
         d = np.linalg.norm(pos[:, None] - centers[None], axis=2) - radii[None]
         tgt = d.min(1, keepdims=True).astype(np.float32)
         la.append(tr.training_step(pos, tgt))
         lb.append(ot.training_step(pos, tgt))
-    a, b = np.mean(la[-50:]), np.mean(lb[-50:])
+    a, b = np.mean(la[-200:]), np.mean(lb[-200:])
     assert abs(a - b) <= 0.02 * b, (a, b)
     assert a < 0.5 * np.mean(la[:10])
     tr.close()

@@ -816,13 +816,10 @@ int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   P.loss_acc = loss_acc;
   P.inv_N = inv_N;
   // dY scale: a power of two near 1/inv_N (the batch), so fp16 dY ~ O(1)
+  // (external gradients of a mean loss have the same 1/batch magnitude).
   int e = 0;
-  if (dext) {
-    P.dscale = 1.0f;
-  } else {
-    frexpf(inv_N > 0.f ? 1.0f / inv_N : 1.0f, &e);
-    P.dscale = ldexpf(1.0f, e - 1);
-  }
+  frexpf(dext ? (float)(N > 0 ? N : 1) : (inv_N > 0.f ? 1.0f / inv_N : 1.0f), &e);
+  P.dscale = ldexpf(1.0f, e - 1);
   P.inv_dscale = 1.0f / P.dscale;
   P.N = N;
   P.mode = dext ? 1 : 0;

@@ -438,6 +438,69 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
   }
 }
 
+// Hash part of the same update, four elements per thread with 16-byte
+// accesses (the table size L*T*F is a multiple of 4).  Same arithmetic per
+// element as k_adam.
+__global__ void __launch_bounds__(256)
+    k_adam_hash4(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
+                 float *__restrict__ v, int32_t *gh_fixed, float *gh_float,
+                 uint8_t *__restrict__ touched, __half *table_h) {
+  const uint64_t n4 = a.hash_count / 4;
+  for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+       q += (uint64_t)gridDim.x * blockDim.x) {
+    bool on[4] = {true, true, true, true};
+    if (a.sparse) {
+      if (a.entry_width == 2) {
+        uchar2 tt = reinterpret_cast<uchar2 *>(touched)[q];
+        on[0] = on[1] = tt.x != 0;
+        on[2] = on[3] = tt.y != 0;
+        if (tt.x | tt.y) reinterpret_cast<uchar2 *>(touched)[q] = make_uchar2(0, 0);
+      } else {
+        uchar4 tt = reinterpret_cast<uchar4 *>(touched)[q];
+        on[0] = tt.x != 0;
+        on[1] = tt.y != 0;
+        on[2] = tt.z != 0;
+        on[3] = tt.w != 0;
+        if (tt.x | tt.y | tt.z | tt.w)
+          reinterpret_cast<uchar4 *>(touched)[q] = make_uchar4(0, 0, 0, 0);
+      }
+    }
+    float g[4];
+    if (a.grad_fixed) {
+      const int4 gi = reinterpret_cast<int4 *>(gh_fixed)[q];
+      g[0] = (float)gi.x * kInvGradScale;
+      g[1] = (float)gi.y * kInvGradScale;
+      g[2] = (float)gi.z * kInvGradScale;
+      g[3] = (float)gi.w * kInvGradScale;
+      if (gi.x | gi.y | gi.z | gi.w)
+        reinterpret_cast<int4 *>(gh_fixed)[q] = make_int4(0, 0, 0, 0);
+    } else {
+      const float4 gf = reinterpret_cast<float4 *>(gh_float)[q];
+      g[0] = gf.x;
+      g[1] = gf.y;
+      g[2] = gf.z;
+      g[3] = gf.w;
+      if (gf.x != 0.f || gf.y != 0.f || gf.z != 0.f || gf.w != 0.f)
+        reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (!(on[0] | on[1] | on[2] | on[3])) continue;
+    float4 wv = reinterpret_cast<float4 *>(w)[q];
+    float4 mv = reinterpret_cast<float4 *>(m)[q];
+    float4 vv = reinterpret_cast<float4 *>(v)[q];
+    float *pw = &wv.x, *pm = &mv.x, *pv = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (on[k]) adam_elem(pw[k], pm[k], pv[k], g[k], a.lr_hash, a, a.l1_hash, false);
+    reinterpret_cast<float4 *>(w)[q] = wv;
+    reinterpret_cast<float4 *>(m)[q] = mv;
+    reinterpret_cast<float4 *>(v)[q] = vv;
+    if (table_h) {
+      __half2 h[2] = {__floats2half2_rn(wv.x, wv.y), __floats2half2_rn(wv.z, wv.w)};
+      reinterpret_cast<uint2 *>(table_h)[q] = *reinterpret_cast<uint2 *>(h);
+    }
+  }
+}
+
 __global__ void k_to_half(const float *__restrict__ src, __half *dst,
                           uint64_t n) {
   for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -632,12 +695,21 @@ void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
                  int32_t *gh_fixed, float *gh_float, float *gm,
                  uint8_t *touched, __half *table_h, int num_sms,
                  cudaStream_t st) {
-  const uint64_t total = a.slots + a.mlp_count;
-  uint64_t blocks = (total + 255) / 256;
-  const uint64_t cap = (uint64_t)num_sms * 16;
+  // hash table: 4 elements per thread, enough threads to keep HBM busy
+  const uint64_t n4 = a.hash_count / 4;
+  uint64_t blocks = (n4 + 255) / 256;
+  const uint64_t cap = (uint64_t)num_sms * 64;
   if (blocks > cap) blocks = cap;
-  k_adam<<<(unsigned)blocks, 256, 0, st>>>(a, w, m, v, gh_fixed, gh_float, gm,
-                                           touched, table_h);
+  if (blocks)
+    k_adam_hash4<<<(unsigned)blocks, 256, 0, st>>>(a, w, m, v, gh_fixed,
+                                                   gh_float, touched, table_h);
+  // MLP weights: one thread each (slots = 0 selects the MLP range)
+  AdamArgs am = a;
+  am.slots = 0;
+  const uint64_t mb = (a.mlp_count + 255) / 256;
+  if (mb)
+    k_adam<<<(unsigned)mb, 256, 0, st>>>(am, w, m, v, gh_fixed, gh_float, gm,
+                                         touched, table_h);
 }
 
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,

@@ -502,7 +502,7 @@ void adam(tmnn_ctx &c) {
   a.grad_fixed = c.nd.grad_fixed;
   launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
               c.touched.p, c.table_h.p, c.num_sms, c.stream);
-  c.launches++;
+  c.launches += 2;
   fused_weights_changed(c.fws);
   if (!c.sparse)  // the dense path leaves the touched map unused
     CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
