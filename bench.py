@@ -132,7 +132,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -299,8 +299,8 @@ def run_reference(args, w):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="sdf3d", choices=sorted(WORKLOADS))
     ap.add_argument("--family", default="Auto")
@@ -339,12 +339,12 @@ def main():
     stream = torch.cuda.ExternalStream(tr.stream())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
+    clocks = ClockSampler(local)
+    clocks.start()  # sampling covers warm-up (clocks ramp) and timed steps
     for i in range(args.warmup):
         tr.training_step(*pool[i % 4])
-    clocks = ClockSampler(local)
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     l0 = tr.launch_count()
     fb, ad, ar, so, losses = [], [], [], [], []
     ev0.record(stream)
