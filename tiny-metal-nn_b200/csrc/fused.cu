@@ -84,10 +84,11 @@ Layout make_layout(const NetDims &nd, bool train) {
     off = align128(off + kTile * L.hc * 2);
   }
   if (train) {
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < (H > 1 ? 2 : 1); ++k) {
       L.dh[k] = off;
       off = align128(off + kTile * W * 2);
     }
+    if (H == 1) L.dh[1] = L.dh[0];  // no ping-pong without hidden layers
     L.dy = off;
     off = align128(off + kTile * kOutCols * 2);
   }
@@ -768,8 +769,14 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   if (!fn) throw std::runtime_error("fused: no kernel for this shape");
   cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)Ly.total);
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, Ly.total);
+  // CTAs per SM: the tighter of shared memory (1 KB reserved per CTA),
+  // threads and TMEM columns.
+  int dev = 0, smem_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor,
+                         dev);
+  int per_sm = smem_sm / (int)(Ly.total + 1024);
+  if (per_sm > 2048 / kThreads) per_sm = 2048 / kThreads;
   const int tmem_fit = (int)(512 / Ly.tmem_cols);
   if (per_sm > tmem_fit) per_sm = tmem_fit;
   if (per_sm < 1) per_sm = 1;
