@@ -209,6 +209,28 @@ tmnn_status tmnn_cuda_forward_backward(tmnn_ctx *ctx, const float *positions,
                                        const float *targets, uint32_t n,
                                        uint32_t flags, double *loss_sum);
 
+/* forward_backward for callers that cannot allocate device memory at call
+ * time (a framework owning the memory pool, a fixed serving footprint, a
+ * real-time loop that must not stall in the allocator).  No counterpart in
+ * the reference: tmnn has no such entry point.
+ * Same work and result as tmnn_cuda_forward_backward with device pointers
+ * (positions and targets MUST be device pointers), but the scratch the batch
+ * needs (Morton codes, permutation, sorted copies, radix-sort temporary)
+ * lives in one fixed device array inside the library, about 8 MiB, that every
+ * GPU which loads the library keeps until the process exits.  Nothing is
+ * allocated: n is limited to 65536 points and num_outputs to 16; larger
+ * requests fail with TMNN_ERR_INVALID_ARGUMENT.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All calls on a device share the one
+ * array, which keeps the last call's contents; calls that overlap on the GPU
+ * (two contexts on one device driven from two threads) race on it.  With the
+ * FullyFused family, one ordinary training_step or forward_backward must
+ * have run on the context first (it sets up the fused weight image). */
+tmnn_status tmnn_cuda_forward_backward_noalloc(tmnn_ctx *ctx,
+                                               const float *positions,
+                                               const float *targets,
+                                               uint32_t n, double *loss_sum);
+
 /* ITrainerRuntime::forward_for_training (trainer.h:145-149): outputs for an
  * external loss, in input order. */
 tmnn_status tmnn_cuda_forward(tmnn_ctx *ctx, const float *positions,

@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -787,6 +788,107 @@ tmnn_status tmnn_cuda_forward_backward(tmnn_ctx *c, const float *positions,
     const float *p = stage_in(*c, positions, (size_t)n * c->nd.d, c->pos_in, flags);
     const float *t = stage_in(*c, targets, (size_t)n * c->nd.O, c->tgt_in, flags);
     if (c->cfg.morton_sort && n > 1) morton_sort(*c, p, t, n, &p, &t);
+    CK(cudaMemsetAsync(c->loss_acc.p, 0, sizeof(double), c->stream));
+    const uint64_t global_n = (uint64_t)n * (uint64_t)c->world;
+    fwd_bwd(*c, p, t, nullptr, n, global_n ? 1.0f / (float)global_n : 0.0f);
+    CK(cudaMemcpyAsync(c->h_loss, c->loss_acc.p, sizeof(double),
+                       cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    if (loss_sum) *loss_sum = *c->h_loss;
+  });
+}
+
+// ---------------------------------------------------------------------------
+// forward_backward without allocation.
+//
+// Some callers cannot call cudaMalloc at the point where they run a step:
+// code running under a framework's memory pool or a fixed-footprint serving
+// budget, real-time loops that must not stall on the allocator, or hosts that
+// have forbidden device allocation after start-up.  The ordinary
+// tmnn_cuda_forward_backward grows the context's batch staging buffers
+// (Morton codes, permutation, sorted copies, radix-sort temporary) on demand,
+// which allocates.  This variant keeps that scratch in one file-scope device
+// array of fixed size instead, so a call allocates nothing.
+namespace {
+
+constexpr uint32_t kNoAllocMaxPoints = 65536;  // the reference's batch cap
+constexpr uint32_t kNoAllocMaxOutputs = 16;
+constexpr size_t kNoAllocSortTempBytes = 2u << 20;
+constexpr size_t kNoAllocBytes =
+    4 * (size_t)kNoAllocMaxPoints * 4 +                       // codes x2, idx, perm
+    (size_t)kNoAllocMaxPoints * 4 * 4 +                       // sorted positions
+    (size_t)kNoAllocMaxPoints * kNoAllocMaxOutputs * 4 +      // sorted targets
+    kNoAllocSortTempBytes;                                    // radix-sort temp
+
+// Shared by every call on a device; holds the last call's contents.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array for `device` (which must be current).
+// The array's name is a host-side stand-in, so the address is looked up once
+// per device with cudaGetSymbolAddress.
+uint8_t *noalloc_scratch(int device) {
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    throw std::invalid_argument("forward_backward_noalloc: device index too large");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void *p = nullptr;
+    CK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    if (morton_temp_bytes(kNoAllocMaxPoints) > kNoAllocSortTempBytes)
+      throw std::runtime_error(
+          "forward_backward_noalloc: radix-sort temporary exceeds its reserve");
+    g_noalloc_ptr[device] = static_cast<uint8_t *>(p);
+  }
+  return g_noalloc_ptr[device];
+}
+
+}  // namespace
+
+tmnn_status tmnn_cuda_forward_backward_noalloc(tmnn_ctx *c,
+                                               const float *positions,
+                                               const float *targets,
+                                               uint32_t n, double *loss_sum) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (n > 0 && (!positions || !targets))
+      throw std::invalid_argument("forward_backward_noalloc: null arguments");
+    if (n > kNoAllocMaxPoints)
+      throw std::invalid_argument(
+          "forward_backward_noalloc: batch of " + std::to_string(n) +
+          " points exceeds the maximum of 65536 (use tmnn_cuda_forward_backward)");
+    if (c->nd.O > (int)kNoAllocMaxOutputs)
+      throw std::invalid_argument(
+          "forward_backward_noalloc: more than 16 outputs are not supported");
+    if (c->family == TMNN_FAMILY_FULLY_FUSED &&
+        (!c->fws.err || !c->fws.wpack))
+      throw std::invalid_argument(
+          "forward_backward_noalloc: the fused kernel's weight image is not set "
+          "up yet; run one ordinary training_step or forward_backward first");
+    CK(cudaSetDevice(c->device));
+    uint8_t *base = noalloc_scratch(c->device);
+    const size_t N = kNoAllocMaxPoints;
+    uint32_t *codes = reinterpret_cast<uint32_t *>(base);
+    uint32_t *codes_alt = codes + N;
+    uint32_t *idx = codes_alt + N;
+    uint32_t *perm = idx + N;
+    float *pos_s = reinterpret_cast<float *>(perm + N);
+    float *tgt_s = pos_s + N * 4;
+    uint8_t *sort_tmp = reinterpret_cast<uint8_t *>(tgt_s + N * kNoAllocMaxOutputs);
+    const float *p = positions, *t = targets;
+    if (c->cfg.morton_sort && n > 1) {
+      launch_morton_order(p, c->nd.d, n, codes, codes_alt, idx, perm, sort_tmp,
+                          kNoAllocSortTempBytes, c->stream);
+      launch_gather_rows(p, c->nd.d, perm, pos_s, n, c->stream);
+      launch_gather_rows(t, c->nd.O, perm, tgt_s, n, c->stream);
+      c->launches += 4;
+      p = pos_s;
+      t = tgt_s;
+    }
     CK(cudaMemsetAsync(c->loss_acc.p, 0, sizeof(double), c->stream));
     const uint64_t global_n = (uint64_t)n * (uint64_t)c->world;
     fwd_bwd(*c, p, t, nullptr, n, global_n ? 1.0f / (float)global_n : 0.0f);

@@ -91,6 +91,8 @@ _SIGS = [
     ("tmnn_cuda_forward_backward", C.c_int,
      [P, P, P, u32, u32, C.POINTER(C.c_double)]),
     ("tmnn_cuda_read_buffer", C.c_int, [P, C.c_int32, P, C.c_size_t]),
+    ("tmnn_cuda_forward_backward_noalloc", C.c_int,
+     [P, P, P, u32, C.POINTER(C.c_double)]),
     ("tmnn_cuda_forward", C.c_int, [P, P, P, u32, u32]),
     ("tmnn_cuda_zero_grads", C.c_int, [P]),
     ("tmnn_cuda_backward_accumulate", C.c_int, [P, P, P, u32, u32]),
