@@ -74,6 +74,7 @@ struct AdamArgs {
   int32_t entry_width;  // elements per tracked slot
   int32_t sparse;       // update only touched hash slots
   int32_t grad_fixed;
+  int32_t implicit_touch;  // touched = byte set or nonzero float gradient
 };
 
 }  // namespace tmnn

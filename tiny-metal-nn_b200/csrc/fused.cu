@@ -34,7 +34,7 @@ namespace tmnn {
 namespace {
 
 constexpr int kTile = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kMaxTrainHidden = 4;
 constexpr int kOutCols = 16;  // output layer padded to N = 16
 constexpr uint32_t kWaitBound = 1u << 26;
@@ -137,6 +137,8 @@ struct FusedParams {
   uint32_t N;
   uint32_t ntiles;
   int mode;          // 0 internal loss, 1 external dL/dy
+  int implicit_touch; // float gradients: a slot with a nonzero sum is touched;
+                      // only all-zero contributions store the touched byte
 };
 
 // ------------------------------------------------------------- device parts
@@ -299,6 +301,66 @@ __device__ __forceinline__ void load_row16(const __half *tile, int cols, int r,
   }
 }
 
+// 8 fp32 values -> one 16-byte fp16 row segment of a core-blocked tile.
+__device__ __forceinline__ void store_row8(__half *tile, int cols, int r, int c0,
+                                           const float *v) {
+  uint4 u;
+  __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4 *>(tile + tc::cb(r, c0, cols)) = u;
+}
+
+// Interpolated features of NL consecutive levels starting at l0, with all
+// NL * 2^D table loads issued before any is consumed.
+template <int D, int F, bool HALF, int NL>
+__device__ __forceinline__ void encode_levels(const FusedParams &P,
+                                              const float *p, int l0,
+                                              float *out /* [NL*F] */) {
+  const NetDims &nd = P.nd;
+  constexpr int NC = 1 << D;
+  uint32_t offs[NL][NC];
+  float ws[NL][NC];
+#pragma unroll
+  for (int j = 0; j < NL; ++j) {
+    Cell<D> c;
+    cell_of<D>(p, nd.res[l0 + j], c);
+    const uint64_t lb = (uint64_t)(l0 + j) * nd.T * F;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) corner<D, F>(c, k, nd.T - 1u, lb, offs[j][k], ws[j][k]);
+  }
+  float vals[NL][NC][F];
+#pragma unroll
+  for (int j = 0; j < NL; ++j)
+#pragma unroll
+    for (int k = 0; k < NC; ++k) load_entry<F, HALF>(P, offs[j][k], vals[j][k]);
+#pragma unroll
+  for (int j = 0; j < NL; ++j)
+#pragma unroll
+    for (int q = 0; q < F; ++q) {
+      float f = 0.f;
+#pragma unroll
+      for (int k = 0; k < NC; ++k) f = __fadd_rn(f, __fmul_rn(ws[j][k], vals[j][k][q]));
+      out[j * F + q] = f;
+    }
+}
+
+// 8 consecutive fp32 TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// The CTA has 256 threads: thread t and t + 128 share point (row) t % 128.
+// Encode and scatter split the point's levels between the two in 8-column
+// chunks; epilogues split the columns; TMEM lane quarter = warp % 4.
 template <int D, int F, int W, bool HALF, bool TRAIN>
 __global__ void __launch_bounds__(kThreads)
     k_fused(const __grid_constant__ FusedParams P) {
@@ -307,7 +369,12 @@ __global__ void __launch_bounds__(kThreads)
   const Layout &Ly = P.lay;
   const int t = threadIdx.x;
   const int warp = t >> 5;
+  const int r = t & (kTile - 1);   // point row in the tile
+  const int half = t >> 7;         // which half of the work on that row
   const int In = nd.In, H = nd.H, O = nd.O;
+  constexpr int LPC = 8 / F;       // levels per 8-column chunk
+  constexpr int NL = D == 4 ? 1 : (LPC < 2 ? LPC : 2);  // levels per load batch
+  const int n_chunks = In / 8;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(sm + Ly.misc);
   uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + Ly.misc + 8);
   float *s_red = reinterpret_cast<float *>(sm + Ly.misc + 64);  // 16 + 4
@@ -318,11 +385,11 @@ __global__ void __launch_bounds__(kThreads)
     const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage);
     uint4 *dst = reinterpret_cast<uint4 *>(sm);
     for (uint32_t i = t; i < Ly.image_bytes / 16; i += kThreads) dst[i] = src[i];
-    if (TRAIN) {
+    if (TRAIN && half == 0) {
       float ones[16] = {1.f};
-      store_row16(X, Ly.xc, t, In, ones);
+      store_row16(X, Ly.xc, r, In, ones);
       for (int k = 0; k < H; ++k)
-        store_row16(reinterpret_cast<__half *>(sm + Ly.h[k]), Ly.hc, t, W, ones);
+        store_row16(reinterpret_cast<__half *>(sm + Ly.h[k]), Ly.hc, r, W, ones);
     }
     if (t < 20) s_red[t] = 0.f;
     if (t == 0) tc::mbar_init(tc::smem_u32(mbar), 1);
@@ -333,9 +400,8 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tslot;
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t T_s = tmem + Ly.t_scratch;
-  const float *bias0 = reinterpret_cast<const float *>(sm + Ly.b[0]);
   const uint32_t mbar_a = tc::smem_u32(mbar);
   const uint32_t sbase = tc::smem_u32(sm);
   uint32_t phase = 0;
@@ -345,10 +411,10 @@ __global__ void __launch_bounds__(kThreads)
   float db_out[kOutCols];
 #pragma unroll
   for (int m = 0; m < kOutCols; ++m) db_out[m] = 0.f;
-  const uint32_t tmask = nd.T - 1u;
+  // columns of a W-wide epilogue handled by this thread
+  const int c_lo = half * (W / 2), c_hi = c_lo + W / 2;
 
   auto sync_mma = [&]() {
-    // called by every thread after thread 0 committed
     if (!tc::mbar_wait(mbar_a, phase, kWaitBound)) {
       ok = false;
       if (t == 0) atomicExch(P.err, 1);
@@ -357,54 +423,29 @@ __global__ void __launch_bounds__(kThreads)
     tc::fence_after_sync();
   };
   auto publish = [&]() {
-    // shared writes visible to the tensor core; TMEM reads retired
     tc::fence_proxy_async();
     tc::fence_before_sync();
     __syncthreads();
   };
 
   for (uint32_t tile = blockIdx.x; tile < P.ntiles && ok; tile += gridDim.x) {
-    const uint32_t row = tile * kTile + t;
+    const uint32_t row = tile * kTile + r;
     const bool valid = row < P.N;
     float p[4] = {0.f, 0.f, 0.f, 0.f};
     if (valid) {
 #pragma unroll
       for (int a = 0; a < D; ++a) p[a] = __ldg(P.pos + (size_t)row * D + a);
     }
-    // ---- encode
-    {
-      float acc[16];
-      int filled = 0;
-      for (int l = 0; l < nd.L; ++l) {
-        Cell<D> c;
-        cell_of<D>(p, nd.res[l], c);
-        const uint64_t lb = (uint64_t)l * nd.T * F;
-        float f[F];
+    // ---- encode: chunks of 8 feature columns, alternating between halves
+    for (int ch = half; ch < n_chunks; ch += 2) {
+      float acc[8];
 #pragma unroll
-        for (int q = 0; q < F; ++q) f[q] = 0.f;
-        uint32_t offs[1 << D];
-        float ws[1 << D];
-#pragma unroll
-        for (int k = 0; k < (1 << D); ++k) corner<D, F>(c, k, tmask, lb, offs[k], ws[k]);
-        float vals[1 << D][F];
-#pragma unroll
-        for (int k = 0; k < (1 << D); ++k) load_entry<F, HALF>(P, offs[k], vals[k]);
-#pragma unroll
-        for (int k = 0; k < (1 << D); ++k)
-#pragma unroll
-          for (int q = 0; q < F; ++q) f[q] = __fadd_rn(f[q], __fmul_rn(ws[k], vals[k][q]));
-#pragma unroll
-        for (int q = 0; q < F; ++q) acc[filled + q] = f[q];
-        filled += F;
-        if (filled == 16) {
-          store_row16(X, Ly.xc, t, l * F + F - 16, acc);
-          filled = 0;
-        }
-      }
+      for (int j = 0; j < LPC; j += NL)
+        encode_levels<D, F, HALF, NL>(P, p, ch * LPC + j, acc + j * F);
+      store_row8(X, Ly.xc, r, ch * 8, acc);
     }
     publish();
     // ---- forward
-    const int nh_tiles = Ly.n_h_tiles;
     for (int k = 0; k < H; ++k) {
       const int hk = TRAIN ? k : (k & 1);
       const int hp = TRAIN ? k - 1 : ((k - 1) & 1);
@@ -420,18 +461,15 @@ __global__ void __launch_bounds__(kThreads)
       if (!ok) break;
       const float *bk = reinterpret_cast<const float *>(sm + Ly.b[k]);
       __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[hk]);
-#pragma unroll
-      for (int c0 = 0; c0 < W; c0 += 16) {
+      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
         float v[16];
         tc::tmem_ld16(T_s + lane_base + c0, v);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = fmaxf(v[i] + bk[c0 + i], 0.f);
-        store_row16(Hk, Ly.hc, t, c0, v);
+        store_row16(Hk, Ly.hc, r, c0, v);
       }
       publish();
     }
-    (void)nh_tiles;
-    (void)bias0;
     if (!ok) break;
     const int hl = TRAIN ? H - 1 : ((H - 1) & 1);
     // ---- output layer
@@ -443,38 +481,41 @@ __global__ void __launch_bounds__(kThreads)
     }
     sync_mma();
     if (!ok) break;
-    float y[kOutCols];
-    tc::tmem_ld16(T_s + lane_base, y);
-    const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
+    if (half == 0) {
+      float y[kOutCols];
+      tc::tmem_ld16(T_s + lane_base, y);
+      const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
 #pragma unroll
-    for (int m = 0; m < kOutCols; ++m) y[m] += bo[m];
+      for (int m = 0; m < kOutCols; ++m) y[m] += bo[m];
+      if (!TRAIN) {
+        if (valid)
+          for (int m = 0; m < O; ++m) P.out[(size_t)row * O + m] = y[m];
+      } else {
+        // loss / external gradient -> scaled dY in shared memory
+        float d[kOutCols];
+#pragma unroll
+        for (int m = 0; m < kOutCols; ++m) d[m] = 0.f;
+        if (valid) {
+          if (P.mode == 0) {
+            float tg[kOutCols];
+            for (int m = 0; m < O; ++m) tg[m] = __ldg(P.tgt + (size_t)row * O + m);
+            loss_sum += loss_and_grad(nd, y, tg, P.inv_N, d);
+          } else {
+            for (int m = 0; m < O; ++m) d[m] = __ldg(P.dext + (size_t)row * O + m);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < kOutCols; ++m) {
+          db_out[m] += d[m];
+          d[m] *= P.dscale;
+        }
+        store_row16(reinterpret_cast<__half *>(sm + Ly.dy), kOutCols, r, 0, d);
+      }
+    }
     if (!TRAIN) {
-      if (valid)
-        for (int m = 0; m < O; ++m) P.out[(size_t)row * O + m] = y[m];
       tc::fence_before_sync();
       __syncthreads();
       continue;
-    }
-    // ---- loss / external gradient -> dY (scaled) in shared memory
-    {
-      float d[kOutCols];
-#pragma unroll
-      for (int m = 0; m < kOutCols; ++m) d[m] = 0.f;
-      if (valid) {
-        if (P.mode == 0) {
-          float tg[kOutCols];
-          for (int m = 0; m < O; ++m) tg[m] = __ldg(P.tgt + (size_t)row * O + m);
-          loss_sum += loss_and_grad(nd, y, tg, P.inv_N, d);
-        } else {
-          for (int m = 0; m < O; ++m) d[m] = __ldg(P.dext + (size_t)row * O + m);
-        }
-      }
-#pragma unroll
-      for (int m = 0; m < kOutCols; ++m) {
-        db_out[m] += d[m];
-        d[m] *= P.dscale;
-      }
-      store_row16(reinterpret_cast<__half *>(sm + Ly.dy), kOutCols, t, 0, d);
     }
     publish();
     // ---- backward through the output layer
@@ -497,14 +538,13 @@ __global__ void __launch_bounds__(kThreads)
       {
         const __half *Hk = reinterpret_cast<const __half *>(sm + Ly.h[k]);
         __half *dHt = reinterpret_cast<__half *>(sm + Ly.dh[cur]);
-#pragma unroll
-        for (int c0 = 0; c0 < W; c0 += 16) {
+        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
           float v[16], hv[16];
           tc::tmem_ld16(T_s + lane_base + c0, v);
-          load_row16(Hk, Ly.hc, t, c0, hv);
+          load_row16(Hk, Ly.hc, r, c0, hv);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = hv[i] > 0.f ? v[i] : 0.f;
-          store_row16(dHt, W, t, c0, v);
+          store_row16(dHt, W, r, c0, v);
         }
       }
       publish();
@@ -513,16 +553,12 @@ __global__ void __launch_bounds__(kThreads)
         const tc::Operand dHk{sbase + Ly.dh[cur], W, 0};
         const tc::Operand dHkT{sbase + Ly.dh[cur], W, 1};
         if (k > 0) {
-          // D = dH_k . W_k^T  (B = W_k stored [W x W] K-major rows N = i)
           tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[k], W, 0}, kTile, W, W, 0);
-          // dW_k^T += dH_k^T . [H_(k-1) | 1]
           tc::gemm(tmem + Ly.t_dwk[k], dHkT,
                    tc::Operand{sbase + Ly.h[k - 1], Ly.hc, 1}, W, W + 16, kTile,
                    first ? 0u : 1u);
         } else {
-          // dX = dH_0 . W0^T  (B = W0 stored [In x W] K-major rows N = i)
           tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[0], W, 0}, kTile, In, W, 0);
-          // dW0^T += dH_0^T . [X | 1]
           tc::gemm(tmem + Ly.t_dw0, dHkT, tc::Operand{sbase + Ly.x, Ly.xc, 1}, W,
                    In + 16, kTile, first ? 0u : 1u);
         }
@@ -537,15 +573,17 @@ __global__ void __launch_bounds__(kThreads)
     // ---- scatter d_feature * corner weight into the hash gradients
     {
       const int levels = nd.active_levels;
-      for (int l0 = 0; l0 < levels; l0 += 16 / F) {
-        float df[16];
-        tc::tmem_ld16(T_s + lane_base + l0 * F, df);
+      for (int ch = half; ch < n_chunks; ch += 2) {
+        float df[8];
+        tmem_ld8(T_s + lane_base + ch * 8, df);
         if (!valid) continue;
-        const int lend = min(levels, l0 + 16 / F);
-        for (int l = l0; l < lend; ++l) {
+#pragma unroll
+        for (int j = 0; j < LPC; ++j) {
+          const int l = ch * LPC + j;
+          if (l >= levels) break;
           float dfe[F];
 #pragma unroll
-          for (int q = 0; q < F; ++q) dfe[q] = df[(l - l0) * F + q] * P.inv_dscale;
+          for (int q = 0; q < F; ++q) dfe[q] = df[j * F + q] * P.inv_dscale;
           Cell<D> c;
           cell_of<D>(p, nd.res[l], c);
           const uint64_t lb = (uint64_t)l * nd.T * F;
@@ -553,7 +591,7 @@ __global__ void __launch_bounds__(kThreads)
           for (int k = 0; k < (1 << D); ++k) {
             uint32_t off;
             float w;
-            corner<D, F>(c, k, tmask, lb, off, w);
+            corner<D, F>(c, k, nd.T - 1u, lb, off, w);
             if (nd.grad_fixed) {
 #pragma unroll
               for (int q = 0; q < F; ++q)
@@ -566,6 +604,13 @@ __global__ void __launch_bounds__(kThreads)
                             dfe[2 % F] * w, dfe[3 % F] * w);
             } else {
               atomicAdd(P.gh_float + off, dfe[0] * w);
+            }
+            if (P.implicit_touch) {
+              // a nonzero contribution marks the slot through its gradient
+              bool zero = true;
+#pragma unroll
+              for (int q = 0; q < F; ++q) zero = zero && dfe[q] * w == 0.f;
+              if (!zero) continue;
             }
             if (F == 2)
               P.touched[off >> 1] = 1;
@@ -584,43 +629,40 @@ __global__ void __launch_bounds__(kThreads)
   // ---- epilogue: weight gradients, bias of the output layer, loss
   if (TRAIN && !first && ok) {
     tc::fence_after_sync();
-    // M = W: row r of an accumulator lives in lane r (W == 128) or in lane
-    // (r / 16) * 32 + r % 16 (W == 64).
+    // M = W: row rr of an accumulator lives in lane rr (W == 128) or in lane
+    // (rr / 16) * 32 + rr % 16 (W == 64).
     const int lane = t & 31;
     const bool has_row = W == 128 || lane < 16;
-    const int r = W == 128 ? t : warp * 16 + lane;
+    const int rr = W == 128 ? r : (warp & 3) * 16 + lane;
     const float s = P.inv_dscale;
     auto flush = [&](uint32_t tcol, int ncols, auto &&dest) {
-      for (int c0 = 0; c0 < ncols; c0 += 16) {
+      for (int c0 = half * 16; c0 < ncols; c0 += 32) {
         float v[16];
         tc::tmem_ld16(tmem + lane_base + tcol + c0, v);
         if (!has_row) continue;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int c = c0 + i;
-          float *dst = dest(c);
+          float *dst = dest(c0 + i);
           if (dst && v[i] != 0.f) atomicAdd(dst, v[i] * s);
         }
       }
     };
-    // dW0^T[j][i] -> W0[i][j]; column In is the bias gradient of layer 0
     flush(Ly.t_dw0, In + 16, [&](int c) -> float * {
-      if (c < In) return P.gm + nd.w_off[0] + (int64_t)c * W + r;
-      if (c == In) return P.gm + nd.b_off[0] + r;
+      if (c < In) return P.gm + nd.w_off[0] + (int64_t)c * W + rr;
+      if (c == In) return P.gm + nd.b_off[0] + rr;
       return nullptr;
     });
     for (int k = 1; k < H; ++k)
       flush(Ly.t_dwk[k], W + 16, [&](int c) -> float * {
-        if (c < W) return P.gm + nd.w_off[k] + (int64_t)c * W + r;
-        if (c == W) return P.gm + nd.b_off[k] + r;
+        if (c < W) return P.gm + nd.w_off[k] + (int64_t)c * W + rr;
+        if (c == W) return P.gm + nd.b_off[k] + rr;
         return nullptr;
       });
     flush(Ly.t_dwout, kOutCols, [&](int c) -> float * {
-      return c < O ? P.gm + nd.w_off[H] + (int64_t)r * O + c : nullptr;
+      return c < O ? P.gm + nd.w_off[H] + (int64_t)rr * O + c : nullptr;
     });
   }
-  if (TRAIN) {
-    // output bias gradient and loss: warp reduction, then shared, then global
+  if (TRAIN && half == 0) {
 #pragma unroll
     for (int m = 0; m < kOutCols; ++m) {
       float v = db_out[m];
@@ -811,8 +853,10 @@ int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                 const float *params, const __half *table_h, const float *pos,
                 const float *tgt, const float *dext, float inv_N, float *gm,
                 int32_t *gh_fixed, float *gh_float, uint8_t *touched,
-                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st) {
+                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st,
+                bool implicit_touch) {
   FusedParams P{};
+  P.implicit_touch = implicit_touch ? 1 : 0;
   P.pos = pos;
   P.tgt = tgt;
   P.dext = dext;

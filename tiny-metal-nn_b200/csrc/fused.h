@@ -33,7 +33,8 @@ int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                 const float *params, const __half *table_h, const float *pos,
                 const float *tgt, const float *dext, float inv_N, float *gm,
                 int32_t *gh_fixed, float *gh_float, uint8_t *touched,
-                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st);
+                double *loss_acc, uint32_t N, int num_sms, cudaStream_t st,
+                bool implicit_touch);
 int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                   const float *params, const __half *table_h, const float *pos,
                   float *out, uint32_t N, int num_sms, cudaStream_t st);

@@ -482,6 +482,15 @@ __global__ void __launch_bounds__(256)
       g[3] = gf.w;
       if (gf.x != 0.f || gf.y != 0.f || gf.z != 0.f || gf.w != 0.f)
         reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a.sparse && a.implicit_touch) {
+        if (a.entry_width == 2) {
+          on[0] = on[1] = on[0] || g[0] != 0.f || g[1] != 0.f;
+          on[2] = on[3] = on[2] || g[2] != 0.f || g[3] != 0.f;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) on[k] = on[k] || g[k] != 0.f;
+        }
+      }
     }
     if (!(on[0] | on[1] | on[2] | on[3])) continue;
     float4 wv = reinterpret_cast<float4 *>(w)[q];
@@ -499,6 +508,25 @@ __global__ void __launch_bounds__(256)
       reinterpret_cast<uint2 *>(table_h)[q] = *reinterpret_cast<uint2 *>(h);
     }
   }
+}
+
+// Completes the touched map of the implicit-touch mode: a slot whose float
+// gradient is nonzero is touched (read-back only).
+__global__ void k_touched_from_grads(const float *__restrict__ g,
+                                     uint8_t *touched, uint64_t slots, int ew) {
+  for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < slots;
+       s += (uint64_t)gridDim.x * blockDim.x) {
+    bool nz = false;
+    for (int k = 0; k < ew; ++k) nz = nz || g[s * ew + k] != 0.f;
+    if (nz) touched[s] = 1;
+  }
+}
+
+void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
+                               int entry_width, int num_sms, cudaStream_t st) {
+  if (slots)
+    k_touched_from_grads<<<num_sms * 8, 256, 0, st>>>(g, touched, slots,
+                                                      entry_width);
 }
 
 __global__ void k_to_half(const float *__restrict__ src, __half *dst,

@@ -98,6 +98,9 @@ struct tmnn_ctx {
   int fallback_reason = kReasonNone;
   std::string plan_text;
   bool sparse = true;
+  // float gradients of the fused family: a nonzero gradient marks its slot
+  // touched, so the kernel stores touched bytes only for zero contributions
+  bool implicit_touch = false;
   uint32_t step = 0;
   uint64_t launches = 0;
   std::atomic<bool> busy{false};
@@ -437,7 +440,7 @@ void fwd_bwd(tmnn_ctx &c, const float *pos, const float *tgt,
     c.launches += fused_train(c.fws, c.nd, c.spec, c.params.p, c.table_h.p,
                               pos, tgt, dext, inv_N, c.gm.p, c.gh_fixed.p,
                               c.gh_float.p, c.touched.p, c.loss_acc.p, N,
-                              c.num_sms, c.stream);
+                              c.num_sms, c.stream, c.implicit_touch);
     return;
   }
   launch_train_exact(c.nd, c.hash_w(), c.mlp_w(), pos, tgt, dext, inv_N,
@@ -501,6 +504,7 @@ void adam(tmnn_ctx &c) {
   a.entry_width = c.entry_width;
   a.sparse = c.sparse ? 1 : 0;
   a.grad_fixed = c.nd.grad_fixed;
+  a.implicit_touch = c.implicit_touch ? 1 : 0;
   launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
               c.touched.p, c.table_h.p, c.num_sms, c.stream);
   c.launches += 2;
@@ -544,6 +548,8 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   c.m.alloc(total);
   c.v.alloc(total);
   if (spec.table_dtype == TMNN_DTYPE_F16) c.table_h.alloc(c.hash_count);
+  plan_family(c);
+  c.implicit_touch = c.family == TMNN_FAMILY_FULLY_FUSED && !c.nd.grad_fixed;
   if (c.nd.grad_fixed)
     c.gh_fixed.alloc(c.hash_count);
   else
@@ -553,7 +559,6 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   c.loss_acc.alloc(1);
   const size_t sf = exact_scratch_floats(c.nd, c.num_sms);
   if (sf) c.scratch.alloc(sf);
-  plan_family(c);
   init_weights(c);
   refresh_gather_copy(c);
   reset_optimizer(c);
@@ -911,6 +916,9 @@ tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *c, int32_t role, void *host,
     if (!host || bytes != v.bytes)
       throw std::invalid_argument("read_buffer: size mismatch");
     CK(cudaSetDevice(c->device));
+    if (role == TMNN_BUF_TOUCHED && c->implicit_touch)
+      launch_touched_from_grads(c->gh_float.p, c->touched.p, c->slots,
+                                c->entry_width, c->num_sms, c->stream);
     CK(cudaMemcpyAsync(host, v.device_ptr, bytes, cudaMemcpyDeviceToHost,
                        c->stream));
     CK(cudaStreamSynchronize(c->stream));
