@@ -328,7 +328,17 @@ def main():
         import torch.distributed as dist
         uid = [t.dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
-        tr.dp_init(uid[0], rank, world)
+        # NCCL prints its version on stdout at communicator creation; keep
+        # stdout for the single JSON line
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            tr.dp_init(uid[0], rank, world)
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     plan = tr.plan()
     B = w["batch"]
     # device-resident pool of distinct batches (inputs + working set > L2)

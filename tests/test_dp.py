@@ -1,0 +1,164 @@
+"""Data parallelism.
+
+CPU (gloo, world size 2): the design of the data-parallel step -- every rank
+runs forward/backward on its shard with dL/dy scaled by the GLOBAL batch,
+the gradients (int32 fixed point, so the sum is exact) and the touched maps
+(max = OR) are all-reduced, and every rank applies the same Adam -- checked
+with the CPU oracle: the two ranks end bit-identical to one process that
+trains on the concatenated batch.
+
+GPU (2 devices): the library's own NCCL path, tmnn_cuda_dp_init + training
+steps on two GPUs, against one GPU on the concatenated batch."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+KW = dict(L=4, F=2, log2T=10, W=16, H=1, O=1, loss=0)
+# the tensor-core family needs levels x features to be a multiple of 16
+KW_FUSED = dict(L=8, F=2, log2T=10, W=64, H=1, O=1, loss=0)
+
+
+def _data(steps=3, n=512):
+    rng = np.random.default_rng(21)
+    out = []
+    for _ in range(steps):
+        pos = rng.uniform(-1, 1, (2 * n, 3)).astype(np.float32)
+        tgt = (np.linalg.norm(pos, axis=1, keepdims=True) - 0.5).astype(np.float32)
+        out.append((pos, tgt))
+    return out
+
+
+def _gloo_rank(rank, world, port, q, steps):
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")):
+        sys.path.insert(0, p)
+    import oracle as o
+    from _util import oracle_spec
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    s = oracle_spec(**KW)
+    hw, mw = o.init_weights(s, seed=5)
+    w = np.concatenate([hw, mw])
+    m, v = np.zeros_like(w), np.zeros_like(w)
+    for step, (pos, tgt) in enumerate(_data(steps)):
+        n = pos.shape[0] // world
+        sl = slice(rank * n, (rank + 1) * n)
+        g = o.zero_grads(s)
+        o.fwd_bwd(s, w[:hw.size].copy(), w[hw.size:].copy(), pos[sl], tgt[sl],
+                  inv_count=pos.shape[0], grads=g)
+        for key, op in (("hash_fixed", dist.ReduceOp.SUM),
+                        ("mlp", dist.ReduceOp.SUM),
+                        ("touched", dist.ReduceOp.MAX)):
+            t = torch.from_numpy(g[key].astype(np.int32 if key == "touched" else g[key].dtype))
+            dist.all_reduce(t, op=op)
+            g[key] = t.numpy().astype(g[key].dtype)
+        o.adam(s, w, m, v, g, step)
+    q.put((rank, w))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("steps", [1, 3])
+def test_dp_design_matches_single_process_gloo(steps):
+    """One step: bit-exact (integer gradient sums are order independent).
+    Later steps: the MLP's float gradient sums differ in order between the
+    shard sums and one sum, so the comparison is to fp32 round-off."""
+    import oracle as o
+    from _util import oracle_spec
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, q, steps)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    s = oracle_spec(**KW)
+    hw, mw = o.init_weights(s, seed=5)
+    w = np.concatenate([hw, mw])
+    m, v = np.zeros_like(w), np.zeros_like(w)
+    for step, (pos, tgt) in enumerate(_data(steps)):
+        g = o.zero_grads(s)
+        o.fwd_bwd(s, w[:hw.size].copy(), w[hw.size:].copy(), pos, tgt, grads=g)
+        o.adam(s, w, m, v, g, step)
+    assert np.array_equal(res[0], res[1])            # replicas agree
+    if steps == 1:
+        assert np.array_equal(res[0][:hw.size], w[:hw.size])   # exact hash part
+    assert np.allclose(res[0][:hw.size], w[:hw.size], rtol=0, atol=1e-6)
+    assert np.allclose(res[0][hw.size:], w[hw.size:], rtol=1e-4, atol=1e-6)
+
+
+def _gpu_rank(rank, world, port, q, family, grad):
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),
+              os.path.join(ROOT, "oracle")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import tmnn_b200 as t
+    from _util import cuda_trainer
+    kw = KW_FUSED if family == "FullyFused" else KW
+    tr = cuda_trainer(**kw, family=family, grad=grad, device=rank)
+    uid = [t.dp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    tr.dp_init(uid[0], rank, world)
+    losses = []
+    for pos, tgt in _data():
+        n = pos.shape[0] // world
+        losses.append(tr.training_step(np.ascontiguousarray(pos[rank * n:(rank + 1) * n]),
+                                       np.ascontiguousarray(tgt[rank * n:(rank + 1) * n])))
+    q.put((rank, tr.weights(), losses))
+    tr.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("family,grad", [("SafeDebug", "Fixed16"), ("FullyFused", "F32")])
+def test_dp_nccl_two_gpus_match_one(family, grad):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from _util import cuda_trainer
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, port, q, family, grad))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, wts, losses = q.get(timeout=120)
+        res[r] = (wts, losses)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = cuda_trainer(**(KW_FUSED if family == "FullyFused" else KW),
+                       family=family, grad=grad)
+    ref_losses = [ref.training_step(p, t) for p, t in _data()]
+    (h0, m0), l0 = res[0]
+    (h1, m1), _ = res[1]
+    hr, mr = ref.weights()
+    assert np.array_equal(h0, h1) and np.array_equal(m0, m1)
+    assert np.allclose(h0, hr, rtol=0, atol=1e-5)
+    assert np.allclose(m0, mr, rtol=1e-3, atol=1e-5)
+    assert np.allclose(l0, ref_losses, rtol=1e-3)
+    ref.close()
