@@ -311,11 +311,20 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = WORKLOADS[args.workload]
+    # NCCL (torch's and the library's) print banners on stdout; stdout is
+    # reserved for the single JSON line, so everything else goes to stderr
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+
+    def emit(obj):
+        os.write(json_fd, (json.dumps(obj) + "\n").encode())
+
     rank, world, local = dist_setup(args)
 
     if args.impl == "reference":
         if rank == 0:
-            print(json.dumps(run_reference(args, w)), flush=True)
+            emit(run_reference(args, w))
         return
 
     import torch
@@ -330,15 +339,7 @@ def main():
         dist.broadcast_object_list(uid, src=0)
         # NCCL prints its version on stdout at communicator creation; keep
         # stdout for the single JSON line
-        sys.stdout.flush()
-        saved = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            tr.dp_init(uid[0], rank, world)
-        finally:
-            sys.stdout.flush()
-            os.dup2(saved, 1)
-            os.close(saved)
+        tr.dp_init(uid[0], rank, world)
     plan = tr.plan()
     B = w["batch"]
     # device-resident pool of distinct batches (inputs + working set > L2)
@@ -471,7 +472,7 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w)
     tr.close()
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 if __name__ == "__main__":

@@ -114,7 +114,12 @@ typedef struct tmnn_train_cfg {
   int32_t morton_sort;          /* 1: Morton-sort every training batch */
   int32_t sparse_hash_adam;     /* -1 auto (sparse iff l1_reg == 0), 0, 1 */
   int32_t active_levels;        /* <= 0: all levels receive gradients */
-  int32_t reserved[7];
+  int32_t dp_replicated_optimizer; /* 1: every rank runs the full Adam after
+                                      one allreduce; 0 (default): from 4
+                                      ranks on, Adam is sharded over the
+                                      ranks (reduce-scatter, Adam on 1/world
+                                      of the table, all-gather) */
+  int32_t reserved[6];
 } tmnn_train_cfg;
 
 /* TrainingStepResult (include/tiny-metal-nn/common.h:97-110), reduced. */
@@ -289,6 +294,15 @@ tmnn_status tmnn_cuda_synchronize(tmnn_ctx *ctx);
 tmnn_status tmnn_cuda_dp_unique_id(uint8_t out[128]);
 tmnn_status tmnn_cuda_dp_init(tmnn_ctx *ctx, const uint8_t unique_id[128],
                               int rank, int world);
+
+/* From 4 ranks on the optimizer is sharded (dp_replicated_optimizer == 0):
+ * each rank keeps the current fp32 table, m and v only for its 1/world shard
+ * (the gather copy the kernels read is always complete).  This collective
+ * call -- every rank must make it -- gathers the shards; until then
+ * get_weights, export_opt_state, debug_encode and reading the weight or
+ * moment buffers fail with TMNN_ERR_INVALID_ARGUMENT.  No reference
+ * counterpart (tmnn is single-device). */
+tmnn_status tmnn_cuda_dp_sync_state(tmnn_ctx *ctx);
 
 /* Message of the last failure on this thread ("" if none). */
 const char *tmnn_cuda_last_error(void);

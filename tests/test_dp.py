@@ -126,6 +126,7 @@ def _gpu_rank(rank, world, port, q, family, grad):
         n = pos.shape[0] // world
         losses.append(tr.training_step(np.ascontiguousarray(pos[rank * n:(rank + 1) * n]),
                                        np.ascontiguousarray(tgt[rank * n:(rank + 1) * n])))
+    tr.dp_sync_state()  # collective; needed when the optimizer is sharded
     q.put((rank, tr.weights(), losses))
     tr.close()
     dist.destroy_process_group()
@@ -136,12 +137,13 @@ def _gpu_rank(rank, world, port, q, family, grad):
 def test_dp_nccl_two_gpus_match_one(family, grad):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    world = 4 if torch.cuda.device_count() >= 4 else 2  # 4: sharded optimizer
     from _util import cuda_trainer
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_rank, args=(r, 2, port, q, family, grad))
-             for r in range(2)]
+    procs = [ctx.Process(target=_gpu_rank, args=(r, world, port, q, family, grad))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}

@@ -137,8 +137,8 @@ struct FusedParams {
   uint32_t N;
   uint32_t ntiles;
   int mode;          // 0 internal loss, 1 external dL/dy
-  int implicit_touch; // float gradients: a slot with a nonzero sum is touched;
-                      // only all-zero contributions store the touched byte
+  int implicit_touch; // float gradients: a slot with a nonzero sum is touched
+                      // (no touched-byte stores)
 };
 
 // ------------------------------------------------------------- device parts
@@ -597,20 +597,31 @@ __global__ void __launch_bounds__(kThreads)
               for (int q = 0; q < F; ++q)
                 atomicAdd(P.gh_fixed + off + q,
                           fixed_trunc(__fmul_rn(__fmul_rn(dfe[q], w), kGradScale)));
-            } else if (F == 2) {
-              red_add_f32x2(P.gh_float + off, dfe[0] * w, dfe[F - 1] * w);
-            } else if (F == 4) {
-              red_add_f32x4(P.gh_float + off, dfe[0] * w, dfe[1 % F] * w,
-                            dfe[2 % F] * w, dfe[3 % F] * w);
             } else {
-              atomicAdd(P.gh_float + off, dfe[0] * w);
-            }
-            if (P.implicit_touch) {
-              // a nonzero contribution marks the slot through its gradient
+              float gv[F];
               bool zero = true;
 #pragma unroll
-              for (int q = 0; q < F; ++q) zero = zero && dfe[q] * w == 0.f;
-              if (!zero) continue;
+              for (int q = 0; q < F; ++q) {
+                gv[q] = dfe[q] * w;
+                zero = zero && gv[q] == 0.f;
+              }
+              if (P.implicit_touch && zero) {
+                // an all-zero contribution still touches its slot: it adds
+                // the smallest subnormal, so the slot's sum is nonzero (Adam
+                // treats a nonzero gradient as touched; 1.4e-45 leaves m and
+                // v unchanged in fp32)
+#pragma unroll
+                for (int q = 0; q < F; ++q)
+                  gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(1);
+              }
+              if (F == 2)
+                red_add_f32x2(P.gh_float + off, gv[0], gv[F - 1]);
+              else if (F == 4)
+                red_add_f32x4(P.gh_float + off, gv[0], gv[1 % F], gv[2 % F],
+                              gv[3 % F]);
+              else
+                atomicAdd(P.gh_float + off, gv[0]);
+              if (P.implicit_touch) continue;
             }
             if (F == 2)
               P.touched[off >> 1] = 1;

@@ -30,6 +30,8 @@ void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
                  cudaStream_t st);
 void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
                                int entry_width, int num_sms, cudaStream_t st);
+void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,
+                     float *gm, int num_sms, cudaStream_t st);
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,
                     cudaStream_t st);
 void launch_init_uniform(float *out, uint64_t count, float low, float high,

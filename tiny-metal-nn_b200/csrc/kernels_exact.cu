@@ -740,6 +740,18 @@ void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
                                          touched, table_h);
 }
 
+// MLP part of the update only (w, m, v, gm indexed from a.hash_count).
+void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,
+                     float *gm, int num_sms, cudaStream_t st) {
+  (void)num_sms;
+  AdamArgs am = a;
+  am.slots = 0;
+  const uint64_t mb = (a.mlp_count + 255) / 256;
+  if (mb)
+    k_adam<<<(unsigned)mb, 256, 0, st>>>(am, w, m, v, nullptr, nullptr, gm,
+                                         nullptr, nullptr);
+}
+
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,
                     cudaStream_t st) {
   if (n == 0) return;

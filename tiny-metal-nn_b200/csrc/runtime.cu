@@ -122,6 +122,10 @@ struct tmnn_ctx {
   // data parallelism
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  // sharded data-parallel optimizer: this rank's copies of the fp32 table
+  // outside its shard, and of m and v outside its shard, are out of date
+  // until tmnn_cuda_dp_sync_state gathers them
+  bool stale = false;
 
   float *hash_w() { return params.p; }
   float *mlp_w() { return params.p + hash_count; }
@@ -472,7 +476,7 @@ void allreduce_grads(tmnn_ctx &c, bool with_loss) {
                      ncclSum, c.comm, c.stream));
   NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
                    c.stream));
-  if (c.sparse)
+  if (c.sparse && !c.implicit_touch)  // implicit: the gradient sum decides
     NK(ncclAllReduce(c.touched.p, c.touched.p, c.slots, ncclUint8, ncclMax,
                      c.comm, c.stream));
   if (with_loss)
@@ -484,7 +488,7 @@ void allreduce_grads(tmnn_ctx &c, bool with_loss) {
 // Adam over the fused [hash | mlp] buffer with the reference's bias
 // corrections bc_k = 1 - pow(beta_k, step + 1) in float (adam_params.h:33-52),
 // then the gradient reset; advances the step counter.
-void adam(tmnn_ctx &c) {
+AdamArgs adam_args(const tmnn_ctx &c) {
   AdamArgs a{};
   const float s = (float)(c.step + 1u);
   a.lr_hash = c.cfg.lr_encoding;
@@ -505,6 +509,11 @@ void adam(tmnn_ctx &c) {
   a.sparse = c.sparse ? 1 : 0;
   a.grad_fixed = c.nd.grad_fixed;
   a.implicit_touch = c.implicit_touch ? 1 : 0;
+  return a;
+}
+
+void adam(tmnn_ctx &c) {
+  const AdamArgs a = adam_args(c);
   launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
               c.touched.p, c.table_h.p, c.num_sms, c.stream);
   c.launches += 2;
@@ -512,6 +521,99 @@ void adam(tmnn_ctx &c) {
   if (!c.sparse)  // the dense path leaves the touched map unused
     CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
   c.step++;
+}
+
+// Data-parallel update with the optimizer sharded over the ranks (ZeRO-1
+// style): reduce-scatter the hash gradients and touched map so each rank
+// owns 1/world of the table, Adam on that shard only (MLP replicated after an
+// allreduce), then all-gather the updated fp32 table.  Same bytes on NVLink
+// as one allreduce, 1/world of the table's Adam work per rank.
+bool can_shard(const tmnn_ctx &c) {
+  // at 2 ranks the extra memsets and fp16 refresh cost more than the halved
+  // Adam saves (measured); from 4 ranks on the sharded update is cheaper
+  return c.comm && c.world >= 4 && c.cfg.dp_replicated_optimizer == 0 &&
+         c.hash_count % (4ull * (uint64_t)c.world) == 0 &&
+         c.slots % (uint64_t)c.world == 0;
+}
+
+void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm) {
+  const size_t shard = c.hash_count / c.world, off = shard * c.rank;
+  const size_t sslots = c.slots / c.world, soff = sslots * c.rank;
+  NK(ncclGroupStart());
+  if (c.nd.grad_fixed)
+    NK(ncclReduceScatter(c.gh_fixed.p, c.gh_fixed.p + off, shard, ncclInt32,
+                         ncclSum, c.comm, c.stream));
+  else
+    NK(ncclReduceScatter(c.gh_float.p, c.gh_float.p + off, shard, ncclFloat32,
+                         ncclSum, c.comm, c.stream));
+  if (c.sparse && !c.implicit_touch)
+    NK(ncclReduceScatter(c.touched.p, c.touched.p + soff, sslots, ncclUint8,
+                         ncclMax, c.comm, c.stream));
+  NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
+                   c.stream));
+  if (with_loss)
+    NK(ncclAllReduce(c.loss_acc.p, c.loss_acc.p, 1, ncclFloat64, ncclSum,
+                     c.comm, c.stream));
+  NK(ncclGroupEnd());
+  if (after_comm) CK(cudaEventRecord(after_comm, c.stream));
+  const AdamArgs a = adam_args(c);
+  AdamArgs ah = a;
+  ah.hash_count = shard;
+  ah.slots = sslots;
+  ah.mlp_count = 0;
+  launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
+              c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
+              c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+              c.touched.p + soff, c.table_h.p ? c.table_h.p + off : nullptr,
+              c.num_sms, c.stream);
+  launch_adam_mlp(a, c.params.p, c.m.p, c.v.p, c.gm.p, c.num_sms, c.stream);
+  c.launches += 2;
+  // other ranks' partial sums outside this rank's shard
+  if (c.gh_fixed.p)
+    CK(cudaMemsetAsync(c.gh_fixed.p, 0, c.gh_fixed.bytes(), c.stream));
+  if (c.gh_float.p)
+    CK(cudaMemsetAsync(c.gh_float.p, 0, c.gh_float.bytes(), c.stream));
+  CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
+  if (c.family == TMNN_FAMILY_FULLY_FUSED && c.table_h.p) {
+    // the fused kernels read only the fp16 gather copy of the table: gather
+    // that (half the bytes); the fp32 master stays sharded until synced
+    NK(ncclAllGather(c.table_h.p + off, c.table_h.p, shard, ncclHalf, c.comm,
+                     c.stream));
+  } else {
+    NK(ncclAllGather(c.params.p + off, c.params.p, shard, ncclFloat32, c.comm,
+                     c.stream));
+    if (c.table_h.p) {
+      launch_to_half(c.params.p, c.table_h.p, c.hash_count, c.num_sms,
+                     c.stream);
+      c.launches++;
+    }
+  }
+  c.stale = true;
+  fused_weights_changed(c.fws);
+  c.step++;
+}
+
+// Collective (every rank): gathers the shards of the fp32 table, m and v so
+// every rank holds the full, current state again.
+void dp_sync_state(tmnn_ctx &c) {
+  if (!c.stale) return;
+  const size_t shard = c.hash_count / c.world, off = shard * c.rank;
+  NK(ncclGroupStart());
+  NK(ncclAllGather(c.params.p + off, c.params.p, shard, ncclFloat32, c.comm,
+                   c.stream));
+  NK(ncclAllGather(c.m.p + off, c.m.p, shard, ncclFloat32, c.comm, c.stream));
+  NK(ncclAllGather(c.v.p + off, c.v.p, shard, ncclFloat32, c.comm, c.stream));
+  NK(ncclGroupEnd());
+  CK(cudaStreamSynchronize(c.stream));
+  c.stale = false;
+}
+
+void require_synced(const tmnn_ctx &c, const char *what) {
+  if (c.stale)
+    throw std::invalid_argument(
+        std::string(what) +
+        ": the data-parallel optimizer is sharded; call tmnn_cuda_dp_sync_state "
+        "on every rank first");
 }
 
 void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
@@ -585,10 +687,14 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
   if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
   fwd_bwd(c, p, t, nullptr, N, inv_N);
   if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
-  allreduce_grads(c, true);
-  if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
   const uint32_t done = c.step;
-  adam(c);
+  if (can_shard(c)) {
+    dp_update(c, true, prof ? c.ev[3] : nullptr);
+  } else {
+    allreduce_grads(c, true);
+    if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
+    adam(c);
+  }
   if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
   CK(cudaMemcpyAsync(c.h_loss, c.loss_acc.p, sizeof(double),
                      cudaMemcpyDeviceToHost, c.stream));
@@ -747,6 +853,7 @@ tmnn_status tmnn_cuda_set_initial_weights(tmnn_ctx *c, const float *hash,
     reset_optimizer(*c);
     zero_grads(*c);
     CK(cudaStreamSynchronize(c->stream));
+    if (hash) c->stale = false;  // full table written, moments reset
   });
 }
 
@@ -759,6 +866,7 @@ tmnn_status tmnn_cuda_get_weights(tmnn_ctx *c, float *hash, size_t hash_count,
       throw std::invalid_argument("get_weights: hash count mismatch");
     if (mlp && mlp_count != c->mlp_count)
       throw std::invalid_argument("get_weights: mlp count mismatch");
+    require_synced(*c, "get_weights");
     CK(cudaSetDevice(c->device));
     if (hash)
       CK(cudaMemcpyAsync(hash, c->hash_w(), hash_count * 4,
@@ -915,6 +1023,9 @@ tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *c, int32_t role, void *host,
     BusyGuard g(c);
     if (!host || bytes != v.bytes)
       throw std::invalid_argument("read_buffer: size mismatch");
+    if (role == TMNN_BUF_HASH_WEIGHTS || role == TMNN_BUF_FUSED_WEIGHTS ||
+        role == TMNN_BUF_FUSED_M || role == TMNN_BUF_FUSED_V)
+      require_synced(*c, "read_buffer");
     CK(cudaSetDevice(c->device));
     if (role == TMNN_BUF_TOUCHED && c->implicit_touch)
       launch_touched_from_grads(c->gh_float.p, c->touched.p, c->slots,
@@ -959,8 +1070,12 @@ tmnn_status tmnn_cuda_adam_step(tmnn_ctx *c) {
   return guarded([&] {
     BusyGuard g(c);
     CK(cudaSetDevice(c->device));
-    allreduce_grads(*c, false);
-    adam(*c);
+    if (can_shard(*c)) {
+      dp_update(*c, false, nullptr);
+    } else {
+      allreduce_grads(*c, false);
+      adam(*c);
+    }
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaGetLastError());
   });
@@ -983,6 +1098,7 @@ tmnn_status tmnn_cuda_debug_encode(tmnn_ctx *c, const float *positions,
     BusyGuard g(c);
     if (n > 0 && (!positions || !features))
       throw std::invalid_argument("debug_encode: null arguments");
+    require_synced(*c, "debug_encode");
     CK(cudaSetDevice(c->device));
     ensure_batch(*c, n);
     const float *p = stage_in(*c, positions, (size_t)n * c->nd.d, c->pos_in, 0);
@@ -1015,6 +1131,7 @@ tmnn_status tmnn_cuda_export_opt_state(tmnn_ctx *c, uint8_t *buf, size_t cap,
   return guarded([&] {
     BusyGuard g(c);
     if (!len) throw std::invalid_argument("export_opt_state: null len");
+    require_synced(*c, "export_opt_state");
     const size_t hb = c->hash_count * 4, mb = (size_t)c->mlp_count * 4;
     if (hb > 0xFFFFFFFFull)
       throw CapacityError("export_opt_state: section exceeds u32 length");
@@ -1185,6 +1302,15 @@ tmnn_status tmnn_cuda_dp_unique_id(uint8_t out[128]) {
     ncclUniqueId id;
     NK(ncclGetUniqueId(&id));
     std::memcpy(out, &id, 128);
+  });
+}
+
+tmnn_status tmnn_cuda_dp_sync_state(tmnn_ctx *c) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    CK(cudaSetDevice(c->device));
+    dp_sync_state(*c);
   });
 }
 

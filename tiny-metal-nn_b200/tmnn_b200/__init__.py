@@ -348,6 +348,12 @@ class Trainer:
         _check(lib.tmnn_cuda_launch_count(self._handle(), C.byref(n)))
         return n.value
 
+    def dp_sync_state(self):
+        """Collective: gather the sharded optimizer state on every rank."""
+        h = self._handle()
+        self._guarded(lambda: _check(lib.tmnn_cuda_dp_sync_state(h),
+                                     "dp_sync_state"))
+
     def dp_init(self, unique_id: bytes, rank: int, world: int):
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
         h = self._handle()

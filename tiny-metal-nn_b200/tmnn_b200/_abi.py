@@ -49,7 +49,8 @@ class TrainCfg(C.Structure):
                 ("seed", C.c_uint64), ("family", C.c_int32),
                 ("hash_grad_format", C.c_int32), ("morton_sort", C.c_int32),
                 ("sparse_hash_adam", C.c_int32), ("active_levels", C.c_int32),
-                ("reserved", C.c_int32 * 7)]
+                ("dp_replicated_optimizer", C.c_int32),
+                ("reserved", C.c_int32 * 6)]
 
 
 class StepResult(C.Structure):
@@ -110,6 +111,7 @@ _SIGS = [
     ("tmnn_cuda_synchronize", C.c_int, [P]),
     ("tmnn_cuda_dp_unique_id", C.c_int, [P]),
     ("tmnn_cuda_dp_init", C.c_int, [P, P, C.c_int, C.c_int]),
+    ("tmnn_cuda_dp_sync_state", C.c_int, [P]),
     ("tmnn_cuda_last_error", C.c_char_p, []),
     ("tmnn_cuda_launch_count", C.c_int, [P, C.POINTER(C.c_uint64)]),
 ]
