@@ -304,6 +304,25 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *ctx, const uint8_t unique_id[128],
  * counterpart (tmnn is single-device). */
 tmnn_status tmnn_cuda_dp_sync_state(tmnn_ctx *ctx);
 
+/* Standalone FullyFusedMLP inference (include/tiny-metal-nn/fully_fused_mlp.h
+ * evaluated without an input encoding): ReLU hidden layers, linear outputs,
+ * weights in the reference layout (mlp_kernel_emitter.cpp:163-191),
+ * Xavier-uniform Philox init.  Inputs are fp16 device arrays [n x n_input]
+ * (16-byte aligned), outputs fp32 device arrays [n x n_output].
+ * n_input a multiple of 16 up to 128; width 16/32/64/128; n_output <= 16. */
+typedef struct tmnn_mlp tmnn_mlp;
+tmnn_status tmnn_cuda_mlp_create(int device, uint32_t n_input, uint32_t width,
+                                 uint32_t hidden_layers, uint32_t n_output,
+                                 uint64_t seed, tmnn_mlp **out);
+tmnn_status tmnn_cuda_mlp_destroy(tmnn_mlp *mlp);
+/* Host weights in (set) and/or out (get); count = total weight count. */
+tmnn_status tmnn_cuda_mlp_weights(tmnn_mlp *mlp, const float *host_in,
+                                  float *host_out, size_t count);
+tmnn_status tmnn_cuda_mlp_forward(tmnn_mlp *mlp, const void *input_f16,
+                                  float *output, uint32_t n);
+tmnn_status tmnn_cuda_mlp_stream(tmnn_mlp *mlp, void **stream);
+const char *tmnn_cuda_mlp_last_error(void);
+
 /* Message of the last failure on this thread ("" if none). */
 const char *tmnn_cuda_last_error(void);
 /* Kernels launched by this context since creation (instrumentation). */

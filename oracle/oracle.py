@@ -68,6 +68,7 @@ def _load():
     lib.tmo_hash4.argtypes = [C.c_int32] * 4 + [C.c_uint32]
     lib.tmo_encode.argtypes = [sp, P, P, C.c_int64, P, P, P]
     lib.tmo_forward.argtypes = [sp, P, P, P, C.c_int64, P]
+    lib.tmo_mlp_forward.argtypes = [sp, P, P, C.c_int64, P]
     lib.tmo_fwd_bwd.restype = C.c_double
     lib.tmo_fwd_bwd.argtypes = [sp, P, P, P, P, P, C.c_int64, C.c_int64, P, P,
                                 P, P, P]
@@ -144,6 +145,14 @@ def forward(s, table, mlp, pos):
     out = np.zeros((pos.shape[0], s.O), np.float32)
     lib.tmo_forward(C.byref(s), _p(table), _p(mlp), _p(pos), pos.shape[0],
                     _p(out))
+    return out
+
+
+def mlp_forward(s, mlp, x):
+    """Plain MLP on features x [N x L*F] (use L = n_input, F = 1)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros((x.shape[0], s.O), np.float32)
+    lib.tmo_mlp_forward(C.byref(s), _p(mlp), _p(x), x.shape[0], _p(out))
     return out
 
 

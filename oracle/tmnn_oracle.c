@@ -866,3 +866,44 @@ void tmo_morton_order(const float *pos, int64_t N, int d, uint32_t *perm) {
   qsort(perm, (size_t)N, sizeof(uint32_t), cmp_code);
   free(codes);
 }
+
+/* ------------------------------------------------- plain MLP (no encoding) */
+
+/* FullyFusedMLP evaluated on given input features x [N x In] (In = L*F):
+ * the layer loops of forward_point (mlp_kernel_emitter.cpp:362-480) without
+ * the hash encode.  With fp16_operands the inputs, weights and activations
+ * are rounded to fp16 as a tensor-core kernel consumes them. */
+void tmo_mlp_forward(const tmo_spec *s, const float *mlp, const float *x,
+                     int64_t N, float *out) {
+  offsets_t o;
+  mlp_offsets(s, &o);
+  const int In = s->L * s->F, W = s->W, e = s->fp16_operands;
+#pragma omp parallel for schedule(static)
+  for (int64_t n = 0; n < N; ++n) {
+    float a[MAX_W], b[MAX_W];
+    const float *xi = x + n * In;
+    for (int j = 0; j < W; ++j) {
+      float acc = 0.0f;
+      for (int i = 0; i < In; ++i)
+        acc = acc + r16(e, xi[i]) * r16(e, mlp[o.w_off[0] + (int64_t)i * W + j]);
+      const float t = acc + mlp[o.b_off[0] + j];
+      a[j] = r16(e, t > 0.0f ? t : 0.0f);
+    }
+    for (int k = 1; k < s->H; ++k) {
+      for (int j = 0; j < W; ++j) {
+        float acc = 0.0f;
+        for (int i = 0; i < W; ++i)
+          acc = acc + a[i] * r16(e, mlp[o.w_off[k] + (int64_t)i * W + j]);
+        const float t = acc + mlp[o.b_off[k] + j];
+        b[j] = r16(e, t > 0.0f ? t : 0.0f);
+      }
+      for (int j = 0; j < W; ++j) a[j] = b[j];
+    }
+    for (int m = 0; m < s->O; ++m) {
+      float acc = mlp[o.b_off[s->H] + m];
+      for (int j = 0; j < W; ++j)
+        acc = acc + a[j] * r16(e, mlp[o.w_off[s->H] + (int64_t)j * s->O + m]);
+      out[n * s->O + m] = acc;
+    }
+  }
+}

@@ -69,6 +69,10 @@ void tmo_encode(const tmo_spec *s, const float *table, const float *pos,
 void tmo_forward(const tmo_spec *s, const float *table, const float *mlp,
                  const float *pos, int64_t N, float *out);
 
+/* Plain MLP on given features x [N x L*F] (no encoding). */
+void tmo_mlp_forward(const tmo_spec *s, const float *mlp, const float *x,
+                     int64_t N, float *out);
+
 /* ---- training --------------------------------------------------------- */
 /* One fused forward+backward over N points (the scalar train kernel).
  * inv_count: divisor used for dL/dy (the kernel's inv_N); pass the global

@@ -44,6 +44,11 @@ struct Layout {
   uint32_t w[kMaxHidden + 1];  // W0, W1..W(H-1), Wout (core-blocked fp16)
   uint32_t b[kMaxHidden + 1];  // fp32 biases (bout padded to 16)
   uint32_t image_bytes;
+  // shared-memory homes of the weights and biases; with stream_w the hidden
+  // weight matrices are copied per layer into two alternating slots
+  uint32_t sw[kMaxHidden + 1], sb[kMaxHidden + 1];
+  uint32_t tail_src, tail_dst, tail_bytes;
+  int stream_w;
   // activation tiles
   uint32_t x, h[kMaxHidden], dh[2], dy, misc;
   uint32_t total;
@@ -55,7 +60,7 @@ struct Layout {
 
 inline uint32_t align128(uint32_t v) { return (v + 127u) & ~127u; }
 
-Layout make_layout(const NetDims &nd, bool train) {
+Layout make_layout(const NetDims &nd, bool train, bool stream = false) {
   Layout L{};
   const int In = nd.In, W = nd.W, H = nd.H;
   uint32_t off = 0;
@@ -74,6 +79,24 @@ Layout make_layout(const NetDims &nd, bool train) {
   L.b[H] = off;
   off = align128(off + kOutCols * 4);
   L.image_bytes = off;
+  L.stream_w = stream ? 1 : 0;
+  if (!stream) {
+    for (int k = 0; k <= H; ++k) {
+      L.sw[k] = L.w[k];
+      L.sb[k] = L.b[k];
+    }
+    L.tail_src = L.tail_dst = 0;
+    L.tail_bytes = L.image_bytes;
+  } else {
+    const uint32_t slot = align128((uint32_t)(In > W ? In : W) * W * 2);
+    for (int k = 0; k < H; ++k) L.sw[k] = (uint32_t)(k & 1) * slot;
+    L.tail_src = L.w[H];
+    L.tail_dst = 2 * slot;
+    L.tail_bytes = L.image_bytes - L.w[H];
+    L.sw[H] = L.tail_dst;
+    for (int k = 0; k <= H; ++k) L.sb[k] = L.tail_dst + (L.b[k] - L.w[H]);
+    off = L.tail_dst + L.tail_bytes;
+  }
   L.xc = train ? In + 16 : In;
   L.hc = train ? W + 16 : W;
   L.x = off;
@@ -112,6 +135,7 @@ Layout make_layout(const NetDims &nd, bool train) {
   uint32_t alloc = 32;
   while (alloc < col) alloc <<= 1;
   L.tmem_cols = alloc;
+  if (!train && !stream && L.total > 200 * 1024) return make_layout(nd, train, true);
   return L;
 }
 
@@ -119,6 +143,7 @@ struct FusedParams {
   NetDims nd;
   Layout lay;
   const float *pos;
+  const __half *xin;  // D == 0: fp16 input features [N x In] (no encoding)
   const float *tgt;
   const float *dext;
   float *out;
@@ -382,9 +407,9 @@ __global__ void __launch_bounds__(kThreads)
 
   // ---- prologue: weights to shared, ones columns, barrier, TMEM
   {
-    const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage);
-    uint4 *dst = reinterpret_cast<uint4 *>(sm);
-    for (uint32_t i = t; i < Ly.image_bytes / 16; i += kThreads) dst[i] = src[i];
+    const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage + Ly.tail_src);
+    uint4 *dst = reinterpret_cast<uint4 *>(sm + Ly.tail_dst);
+    for (uint32_t i = t; i < Ly.tail_bytes / 16; i += kThreads) dst[i] = src[i];
     if (TRAIN && half == 0) {
       float ones[16] = {1.f};
       store_row16(X, Ly.xc, r, In, ones);
@@ -411,8 +436,6 @@ __global__ void __launch_bounds__(kThreads)
   float db_out[kOutCols];
 #pragma unroll
   for (int m = 0; m < kOutCols; ++m) db_out[m] = 0.f;
-  // columns of a W-wide epilogue handled by this thread
-  const int c_lo = half * (W / 2), c_hi = c_lo + W / 2;
 
   auto sync_mma = [&]() {
     if (!tc::mbar_wait(mbar_a, phase, kWaitBound)) {
@@ -436,32 +459,49 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
       for (int a = 0; a < D; ++a) p[a] = __ldg(P.pos + (size_t)row * D + a);
     }
-    // ---- encode: chunks of 8 feature columns, alternating between halves
-    for (int ch = half; ch < n_chunks; ch += 2) {
-      float acc[8];
+    if constexpr (D == 0) {
+      // plain MLP: the input features come from memory (fp16)
+      for (int ch = half; ch < n_chunks; ch += 2) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (valid)
+          u = __ldg(reinterpret_cast<const uint4 *>(P.xin + (size_t)row * In) + ch);
+        *reinterpret_cast<uint4 *>(X + tc::cb(r, ch * 8, Ly.xc)) = u;
+      }
+    } else {
+      // ---- encode: chunks of 8 feature columns, alternating between halves
+      for (int ch = half; ch < n_chunks; ch += 2) {
+        float acc[8];
 #pragma unroll
-      for (int j = 0; j < LPC; j += NL)
-        encode_levels<D, F, HALF, NL>(P, p, ch * LPC + j, acc + j * F);
-      store_row8(X, Ly.xc, r, ch * 8, acc);
+        for (int j = 0; j < LPC; j += NL)
+          encode_levels<D, F, HALF, NL>(P, p, ch * LPC + j, acc + j * F);
+        store_row8(X, Ly.xc, r, ch * 8, acc);
+      }
     }
     publish();
     // ---- forward
     for (int k = 0; k < H; ++k) {
       const int hk = TRAIN ? k : (k & 1);
       const int hp = TRAIN ? k - 1 : ((k - 1) & 1);
+      if (!TRAIN && Ly.stream_w) {
+        const uint32_t bytes = (uint32_t)(k == 0 ? In : W) * W * 2;
+        const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage + Ly.w[k]);
+        uint4 *dst = reinterpret_cast<uint4 *>(sm + Ly.sw[k]);
+        for (uint32_t i = t; i < bytes / 16; i += kThreads) dst[i] = src[i];
+        publish();
+      }
       if (t == 0) {
         tc::fence_after_sync();
         tc::Operand A = k == 0 ? tc::Operand{sbase + Ly.x, Ly.xc, 0}
                                : tc::Operand{sbase + Ly.h[hp], Ly.hc, 0};
-        tc::Operand B{sbase + Ly.w[k], W, 1};
+        tc::Operand B{sbase + Ly.sw[k], W, 1};
         tc::gemm(T_s, A, B, kTile, W, k == 0 ? In : W, 0);
         tc::commit(mbar_a);
       }
       sync_mma();
       if (!ok) break;
-      const float *bk = reinterpret_cast<const float *>(sm + Ly.b[k]);
+      const float *bk = reinterpret_cast<const float *>(sm + Ly.sb[k]);
       __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[hk]);
-      for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+      for (int c0 = half * 16; c0 < W; c0 += 32) {
         float v[16];
         tc::tmem_ld16(T_s + lane_base + c0, v);
 #pragma unroll
@@ -476,7 +516,7 @@ __global__ void __launch_bounds__(kThreads)
     if (t == 0) {
       tc::fence_after_sync();
       tc::gemm(T_s, tc::Operand{sbase + Ly.h[hl], Ly.hc, 0},
-               tc::Operand{sbase + Ly.w[H], kOutCols, 1}, kTile, kOutCols, W, 0);
+               tc::Operand{sbase + Ly.sw[H], kOutCols, 1}, kTile, kOutCols, W, 0);
       tc::commit(mbar_a);
     }
     sync_mma();
@@ -484,7 +524,7 @@ __global__ void __launch_bounds__(kThreads)
     if (half == 0) {
       float y[kOutCols];
       tc::tmem_ld16(T_s + lane_base, y);
-      const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
+      const float *bo = reinterpret_cast<const float *>(sm + Ly.sb[H]);
 #pragma unroll
       for (int m = 0; m < kOutCols; ++m) y[m] += bo[m];
       if (!TRAIN) {
@@ -524,7 +564,7 @@ __global__ void __launch_bounds__(kThreads)
       tc::fence_after_sync();
       // dH = dY . Wout^T   (B = Wout stored [W x 16] as K-major rows N = j)
       tc::gemm(T_s, tc::Operand{sbase + Ly.dy, kOutCols, 0},
-               tc::Operand{sbase + Ly.w[H], kOutCols, 0}, kTile, W, kOutCols, 0);
+               tc::Operand{sbase + Ly.sw[H], kOutCols, 0}, kTile, W, kOutCols, 0);
       // dWout += H^T . dY
       tc::gemm(tmem + Ly.t_dwout, tc::Operand{sbase + Ly.h[hl], Ly.hc, 1},
                tc::Operand{sbase + Ly.dy, kOutCols, 1}, W, kOutCols, kTile,
@@ -538,7 +578,7 @@ __global__ void __launch_bounds__(kThreads)
       {
         const __half *Hk = reinterpret_cast<const __half *>(sm + Ly.h[k]);
         __half *dHt = reinterpret_cast<__half *>(sm + Ly.dh[cur]);
-        for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
+        for (int c0 = half * 16; c0 < W; c0 += 32) {
           float v[16], hv[16];
           tc::tmem_ld16(T_s + lane_base + c0, v);
           load_row16(Hk, Ly.hc, r, c0, hv);
@@ -553,12 +593,12 @@ __global__ void __launch_bounds__(kThreads)
         const tc::Operand dHk{sbase + Ly.dh[cur], W, 0};
         const tc::Operand dHkT{sbase + Ly.dh[cur], W, 1};
         if (k > 0) {
-          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[k], W, 0}, kTile, W, W, 0);
+          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.sw[k], W, 0}, kTile, W, W, 0);
           tc::gemm(tmem + Ly.t_dwk[k], dHkT,
                    tc::Operand{sbase + Ly.h[k - 1], Ly.hc, 1}, W, W + 16, kTile,
                    first ? 0u : 1u);
         } else {
-          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.w[0], W, 0}, kTile, In, W, 0);
+          tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.sw[0], W, 0}, kTile, In, W, 0);
           tc::gemm(tmem + Ly.t_dw0, dHkT, tc::Operand{sbase + Ly.x, Ly.xc, 1}, W,
                    In + 16, kTile, first ? 0u : 1u);
         }
@@ -571,7 +611,7 @@ __global__ void __launch_bounds__(kThreads)
     if (!ok) break;
     first = false;
     // ---- scatter d_feature * corner weight into the hash gradients
-    {
+    if constexpr (D > 0) {
       const int levels = nd.active_levels;
       for (int ch = half; ch < n_chunks; ch += 2) {
         float df[8];
@@ -607,12 +647,12 @@ __global__ void __launch_bounds__(kThreads)
               }
               if (P.implicit_touch && zero) {
                 // an all-zero contribution still touches its slot: it adds
-                // the smallest subnormal, so the slot's sum is nonzero (Adam
-                // treats a nonzero gradient as touched; 1.4e-45 leaves m and
-                // v unchanged in fp32)
+                // the smallest normal float 2^-126 (float reductions flush
+                // subnormals), so the slot's sum is nonzero and Adam treats
+                // it as touched; the value is below any weight's ulp
 #pragma unroll
                 for (int q = 0; q < F; ++q)
-                  gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(1);
+                  gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(0x00800000);
               }
               if (F == 2)
                 red_add_f32x2(P.gh_float + off, gv[0], gv[F - 1]);
@@ -743,6 +783,7 @@ KernelFn pick(int d, int F, int W, bool half) {
   TMNN_PICK(3, 1) TMNN_PICK(3, 2) TMNN_PICK(3, 4)
   TMNN_PICK(4, 1) TMNN_PICK(4, 2) TMNN_PICK(4, 4)
 #undef TMNN_PICK
+  if (d == 0 && !TRAIN) return pick_w<0, 2, false, false>(W);
   return nullptr;
 }
 
@@ -757,7 +798,7 @@ bool shape_ok(const NetDims &nd, bool train, std::string *why) {
   if (train) {
     if (nd.W != 64 && nd.W != 128) return no("hidden width must be 64 or 128");
     if (nd.H > kMaxTrainHidden) return no("more than 4 hidden layers");
-  } else if (nd.W % 16 != 0 || nd.W > 128) {
+  } else if (nd.W != 16 && nd.W != 32 && nd.W != 64 && nd.W != 128) {
     return no("hidden width must be 16, 32, 64 or 128");
   }
   const Layout L = make_layout(nd, train);
@@ -897,6 +938,26 @@ int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   P.N = N;
   P.dscale = P.inv_dscale = 1.0f;
   return launch(ws, nd, spec, params, table_h, false, P, num_sms, st);
+}
+
+int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd,
+                      const float *mlp, const __half *x, float *out,
+                      uint32_t N, int num_sms, cudaStream_t st) {
+  FusedParams P{};
+  P.xin = x;
+  P.out = out;
+  P.N = N;
+  P.dscale = P.inv_dscale = 1.0f;
+  tmnn_spec spec{};
+  spec.table_dtype = TMNN_DTYPE_F32;
+  NetDims n0 = nd;
+  n0.d = 0;
+  n0.hash_count = 0;
+  return launch(ws, n0, spec, mlp, nullptr, false, P, num_sms, st);
+}
+
+bool fused_mlp_supported(const NetDims &nd, std::string *why) {
+  return shape_ok(nd, false, why);
 }
 
 int fused_error(FusedWorkspace &ws, cudaStream_t st) {

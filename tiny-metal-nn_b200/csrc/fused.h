@@ -38,6 +38,12 @@ int fused_train(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
 int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                   const float *params, const __half *table_h, const float *pos,
                   float *out, uint32_t N, int num_sms, cudaStream_t st);
+// Plain FullyFusedMLP inference (no encoding): x fp16 [N x nd.In], mlp the
+// fp32 weights in the reference layout, out fp32 [N x nd.O].
+int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
+                      const __half *x, float *out, uint32_t N, int num_sms,
+                      cudaStream_t st);
+bool fused_mlp_supported(const NetDims &nd, std::string *why);
 // Nonzero when a fused kernel reported a timed-out pipeline wait.
 int fused_error(FusedWorkspace &ws, cudaStream_t st);
 

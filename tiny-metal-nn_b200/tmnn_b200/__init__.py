@@ -94,6 +94,68 @@ def _arg(x, name, width):
     return x.ctypes.data_as(C.c_void_p), x.shape[0], 0, x
 
 
+class FullyFusedMLP:
+    """Standalone FullyFusedMLP inference on fp16 device inputs."""
+
+    def __init__(self, n_input, width, hidden_layers, n_output, seed=42,
+                 device=0):
+        h = C.c_void_p()
+        st = lib.tmnn_cuda_mlp_create(device, n_input, width, hidden_layers,
+                                      n_output, seed, C.byref(h))
+        if st != _abi.OK:
+            raise ValueError(lib.tmnn_cuda_mlp_last_error().decode())
+        self._h = h
+        self.n_input, self.n_output = n_input, n_output
+        self.count = (n_input * width + width +
+                      (hidden_layers - 1) * (width * width + width) +
+                      width * n_output + n_output)
+
+    def weights(self):
+        out = np.empty(self.count, np.float32)
+        _check_mlp(lib.tmnn_cuda_mlp_weights(self._h, None,
+                                             out.ctypes.data_as(C.c_void_p),
+                                             self.count))
+        return out
+
+    def set_weights(self, w):
+        w = np.ascontiguousarray(w, np.float32)
+        _check_mlp(lib.tmnn_cuda_mlp_weights(self._h, w.ctypes.data_as(C.c_void_p),
+                                             None, w.size))
+
+    def forward(self, x_f16, out=None):
+        """x_f16: CUDA torch.float16 [n, n_input]; returns fp32 [n, n_output]."""
+        import torch
+        assert x_f16.is_cuda and x_f16.dtype == torch.float16 and x_f16.is_contiguous()
+        n = x_f16.shape[0]
+        if out is None:
+            out = torch.empty((n, self.n_output), dtype=torch.float32,
+                              device=x_f16.device)
+        _check_mlp(lib.tmnn_cuda_mlp_forward(self._h, C.c_void_p(x_f16.data_ptr()),
+                                             C.c_void_p(out.data_ptr()), n))
+        return out
+
+    def stream(self):
+        s = C.c_void_p()
+        _check_mlp(lib.tmnn_cuda_mlp_stream(self._h, C.byref(s)))
+        return s.value
+
+    def close(self):
+        if self._h is not None:
+            lib.tmnn_cuda_mlp_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _check_mlp(st):
+    if st != _abi.OK:
+        raise TmnnError(st, lib.tmnn_cuda_mlp_last_error().decode())
+
+
 def dp_unique_id() -> bytes:
     buf = (C.c_uint8 * 128)()
     _check(lib.tmnn_cuda_dp_unique_id(buf), "dp_unique_id")

@@ -112,6 +112,13 @@ _SIGS = [
     ("tmnn_cuda_dp_unique_id", C.c_int, [P]),
     ("tmnn_cuda_dp_init", C.c_int, [P, P, C.c_int, C.c_int]),
     ("tmnn_cuda_dp_sync_state", C.c_int, [P]),
+    ("tmnn_cuda_mlp_create", C.c_int,
+     [C.c_int, u32, u32, u32, u32, C.c_uint64, C.POINTER(P)]),
+    ("tmnn_cuda_mlp_destroy", C.c_int, [P]),
+    ("tmnn_cuda_mlp_weights", C.c_int, [P, P, P, C.c_size_t]),
+    ("tmnn_cuda_mlp_forward", C.c_int, [P, P, P, u32]),
+    ("tmnn_cuda_mlp_stream", C.c_int, [P, C.POINTER(P)]),
+    ("tmnn_cuda_mlp_last_error", C.c_char_p, []),
     ("tmnn_cuda_last_error", C.c_char_p, []),
     ("tmnn_cuda_launch_count", C.c_int, [P, C.POINTER(C.c_uint64)]),
 ]
