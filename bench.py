@@ -391,6 +391,26 @@ def main():
     inf_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
     inf_sps = world * n_inf * (1 << 20) / (inf_ms / 1000.0)
 
+    # analytic input gradient (single-output fields): value + d/dpos for 2^20
+    # device-resident points per call
+    eg = None
+    if w["O"] == 1:
+        gout = torch.empty((1 << 20, w["d"]), device="cuda")
+        for _ in range(3):
+            tr.evaluate_with_gradient(q, out=out, gradients=gout)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        n_eg = 10
+        l1 = tr.launch_count()
+        for _ in range(n_eg):
+            tr.evaluate_with_gradient(q, out=out, gradients=gout)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        eg_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+        eg = {"samples_per_s": world * n_eg * (1 << 20) / (eg_ms / 1000.0),
+              "ms_per_call": eg_ms / n_eg, "points_per_call": 1 << 20,
+              "launches_per_call": (tr.launch_count() - l1) / n_eg}
+
     # end to end: pinned host inputs through the public API
     e2e = None
     if not args.no_e2e:
@@ -451,6 +471,7 @@ def main():
                          "grads, fp16 gather copy) exceeds the 126 MB L2"},
         "samples_per_s": value * B,
         "inference_samples_per_s": inf_sps,
+        "eval_gradient": eg,
         "final_loss": losses[-1],
         "phase_ms": {"sort": statistics.mean(so), "fwd_bwd": fb_ms,
                      "allreduce": statistics.mean(ar),

@@ -254,6 +254,21 @@ tmnn_status tmnn_cuda_adam_step(tmnn_ctx *ctx);
 tmnn_status tmnn_cuda_evaluate(tmnn_ctx *ctx, const float *positions,
                                float *outputs, uint32_t n, uint32_t flags);
 
+/* Trainer::evaluate_with_gradient / inference_with_gradient
+ * (trainer.h:378-386) -> FieldEvaluator::evaluate_with_gradient
+ * (evaluator.h:45; default_trainer.cpp:467-622) and the EvalGradient kernel
+ * (mlp_kernel_emitter.cpp:1716-2090).  For a single-output network
+ * (num_outputs == 1, else TMNN_ERR_INVALID_ARGUMENT): outputs [n] = the field
+ * value, gradients [n x spatial_dims] = d(value)/d(position), from the fp32
+ * parameters.  The reference returns the two deinterleaved from one
+ * [value, gx, gy, gz] buffer; here they are written separately.  n == 0 is a
+ * no-op; NULL arrays with n > 0 fail like the reference.  Host pointers, or
+ * device pointers with TMNN_PTR_DEVICE. */
+tmnn_status tmnn_cuda_evaluate_with_gradient(tmnn_ctx *ctx,
+                                             const float *positions,
+                                             float *outputs, float *gradients,
+                                             uint32_t n, uint32_t flags);
+
 /* Encoding only (parity instrument): features [n x L*F] f32, and when
  * non-NULL the first table index of every corner [n x L x 2^d] (u32) and the
  * base grid cell [n x L x d] (i32). Host pointers. */

@@ -69,6 +69,7 @@ def _load():
     lib.tmo_encode.argtypes = [sp, P, P, C.c_int64, P, P, P]
     lib.tmo_forward.argtypes = [sp, P, P, P, C.c_int64, P]
     lib.tmo_mlp_forward.argtypes = [sp, P, P, C.c_int64, P]
+    lib.tmo_eval_gradient.argtypes = [sp, P, P, P, C.c_int64, P, P]
     lib.tmo_fwd_bwd.restype = C.c_double
     lib.tmo_fwd_bwd.argtypes = [sp, P, P, P, P, P, C.c_int64, C.c_int64, P, P,
                                 P, P, P]
@@ -154,6 +155,18 @@ def mlp_forward(s, mlp, x):
     out = np.zeros((x.shape[0], s.O), np.float32)
     lib.tmo_mlp_forward(C.byref(s), _p(mlp), _p(x), x.shape[0], _p(out))
     return out
+
+
+def eval_gradient(s, table, mlp, pos):
+    """Field value [N] and d(value)/d(pos) [N x d] of a single-output net."""
+    pos = np.ascontiguousarray(pos, np.float32)
+    N = pos.shape[0]
+    out = np.zeros(N, np.float32)
+    grad = np.zeros((N, s.d), np.float32)
+    lib.tmo_eval_gradient(C.byref(s), _p(np.ascontiguousarray(table, np.float32)),
+                          _p(np.ascontiguousarray(mlp, np.float32)), _p(pos), N,
+                          _p(out), _p(grad))
+    return out, grad
 
 
 def tracked_slots(s):

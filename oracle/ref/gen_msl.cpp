@@ -4,7 +4,7 @@
 // C++ by oracle/ref_build.sh through oracle/ref/metal_shim.h.
 //
 // usage: gen_msl ROLE L F log2T d W H O loss base scale huber active_mask
-//   ROLE: train | eval | fwd | extgrad
+//   ROLE: train | eval | fwd | extgrad | evalgrad
 #include "tiny-metal-nn/kernels/kernel_compiler.h"
 #include <cstdio>
 #include <cstdlib>
@@ -38,6 +38,7 @@ int main(int argc, char **argv) {
   if (!std::strcmp(argv[1], "eval")) role = tmnn::KernelRole::Eval;
   if (!std::strcmp(argv[1], "fwd")) role = tmnn::KernelRole::ForwardForTraining;
   if (!std::strcmp(argv[1], "extgrad")) role = tmnn::KernelRole::BackwardFromExternalGrad;
+  if (!std::strcmp(argv[1], "evalgrad")) role = tmnn::KernelRole::EvalGradient;
   auto r = tmnn::KernelCompiler::compile({role, s, schema, cs});
   std::fprintf(stderr, "entry=%s simd=%d fp16=%d\n", r.entry_point.c_str(),
                (int)r.decision.realized_simd, (int)r.decision.realized_fp16);

@@ -51,6 +51,15 @@ void tmnn_ref_eval(const float *pos, float *out, const float *cfg,
   for (uint32_t t = 0; t < N; ++t)
     ref_k::neural_sdf_eval_points(pos, out, cfg, hash, mlp, t);
 }
+#elif defined(ROLE_EVALGRAD)
+// neural_sdf_analytical_eval_gradient_points: out [N x 4] = value, then the
+// first three position-gradient components.
+void tmnn_ref_eval_gradient(const float *pos, float *out, const float *cfg,
+                            const float *hash, const float *mlp, uint32_t N) {
+  for (uint32_t t = 0; t < N; ++t)
+    ref_k::neural_sdf_analytical_eval_gradient_points(pos, out, cfg, hash, mlp,
+                                                      t);
+}
 #elif defined(ROLE_ADAM)
 // neural_sdf_adam_unified / _hash_sparse / _mlp_dense (USE_INT_ATOMICS_HASH)
 void tmnn_ref_adam_unified(float *w, int32_t *gh, float *gm, float *m,

@@ -35,6 +35,7 @@ SPECS = {
     "sdf": (8, 2, 12, 3, 16, 1, 1, 1, 16.0, 1.447, 1.0),
     "img": (4, 2, 12, 3, 16, 2, 3, 0, 16.0, 1.5, 1.0),
     "d4": (4, 2, 12, 4, 16, 2, 4, 0, 8.0, 1.5, 1.0),
+    "d4o1": (4, 2, 12, 4, 16, 2, 1, 0, 8.0, 1.5, 1.0),
     "f1": (4, 1, 10, 3, 16, 1, 1, 2, 4.0, 2.0, 0.1),
     "f4": (4, 4, 10, 3, 16, 2, 1, 0, 4.0, 2.0, 1.0),
     "h3": (2, 2, 10, 3, 8, 3, 1, 0, 4.0, 2.0, 1.0),
@@ -44,6 +45,13 @@ SPECS = {
     "bench_image": (16, 2, 15, 3, 64, 2, 3, 0, 16.0, 1.5, 1.0),
     "bench_field4d": (16, 2, 22, 4, 64, 2, 4, 0, 8.0, 1.5, 1.0),
 }
+
+
+def float_literals(msl):
+    """Metal has no double: an unsuffixed literal such as `1.0` is a float.
+    Compiled as C++ it would be a double and promote the expression around it,
+    so give every unsuffixed decimal literal an `f` suffix."""
+    return re.sub(r"(?<![\w.])(\d+\.\d*)(?![\w.])", r"\1f", msl)
 
 
 def run(cmd, **kw):
@@ -89,12 +97,17 @@ def build(force=False):
             continue
         args = [str(x) for x in sp]
         objs = []
-        for role, define in (("train", "ROLE_TRAIN"), ("extgrad", "ROLE_EXTGRAD"),
-                             ("eval", "ROLE_EVAL")):
+        roles = [("train", "ROLE_TRAIN"), ("extgrad", "ROLE_EXTGRAD"),
+                 ("eval", "ROLE_EVAL")]
+        if sp[6] == 1:  # the EvalGradient kernel is single-output
+            roles.append(("evalgrad", "ROLE_EVALGRAD"))
+        for role, define in roles:
             msl = os.path.join(OUT, f"{tag}_{role}.msl")
+            text = subprocess.run(
+                [gen, role] + args + ["0" if role.startswith("eval") else "1"],
+                check=True, capture_output=True, text=True).stdout
             with open(msl, "w") as f:
-                run([gen, role] + args + ["1" if role != "eval" else "0"],
-                    stdout=f, stderr=subprocess.DEVNULL)
+                f.write(float_literals(text))
             obj = os.path.join(OUT, f"{tag}_{role}.o")
             run(CXX + shim + ["-c", drv, f"-D{define}",
                               f'-DMSL_FILE="{msl}"', "-o", obj])

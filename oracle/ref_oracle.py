@@ -101,6 +101,23 @@ def evaluate(tag, sp, table, mlp, pos):
     return out
 
 
+def eval_gradient(tag, sp, table, mlp, pos):
+    """The reference's EvalGradient kernel: returns its raw [N x 4] output
+    (value, then d/dx, d/dy, d/dz -- in 4D the fourth component is not
+    written by the kernel)."""
+    L, F, log2T, d, W, H, O = sp[:7]
+    lib = _lib(tag)
+    pos = np.ascontiguousarray(pos, np.float32)
+    N = pos.shape[0]
+    cfg = _config(L, F, log2T, sp[8], sp[9], W, H, N, mlp)
+    out = np.zeros((N, 4), np.float32)
+    lib.tmnn_ref_eval_gradient(_p(pos), _p(out), _p(cfg),
+                               _p(np.ascontiguousarray(table, np.float32)),
+                               _p(np.ascontiguousarray(mlp, np.float32)),
+                               C.c_uint32(N))
+    return out
+
+
 def adam_params(lr_enc, lr_net, b1, b2, eps, l1, l2, hash_size, mlp_count,
                 step, clip=0.0, wd=0.0):
     lib = _lib("host")

@@ -907,3 +907,182 @@ void tmo_mlp_forward(const tmo_spec *s, const float *mlp, const float *x,
     }
   }
 }
+
+/* ------------------------------------------- analytic input gradient */
+
+/* Table value of one corner: hash_grid_lookup (mlp_kernel_emitter.cpp:1663-1671). */
+static float corner_value(const tmo_spec *s, const float *table, int l, int f,
+                          const int32_t *bc, int dx, int dy, int dz, int dw) {
+  const uint32_t T = 1u << s->log2T;
+  const uint32_t h = s->d == 4
+      ? tmo_hash4(bc[0] + dx, bc[1] + dy, bc[2] + dz, bc[3] + dw, T)
+      : tmo_hash3(bc[0] + dx, bc[1] + dy, bc[2] + dz, T);
+  return table[(uint64_t)l * T * s->F + (uint64_t)h * s->F + f];
+}
+
+/* trilinear_feature_grad (mlp_kernel_emitter.cpp:1674-1705): the value by
+ * lerps along x, then y, then z; the three partial derivatives of the
+ * trilinear interpolant w.r.t. the cell fraction. */
+static float trilinear_grad(const tmo_spec *s, const float *table, int l,
+                            int f, const int32_t *bc, const float *fr,
+                            float *g) {
+  const float fx = fr[0], fy = fr[1], fz = fr[2];
+  const float c000 = corner_value(s, table, l, f, bc, 0, 0, 0, 0);
+  const float c001 = corner_value(s, table, l, f, bc, 0, 0, 1, 0);
+  const float c010 = corner_value(s, table, l, f, bc, 0, 1, 0, 0);
+  const float c011 = corner_value(s, table, l, f, bc, 0, 1, 1, 0);
+  const float c100 = corner_value(s, table, l, f, bc, 1, 0, 0, 0);
+  const float c101 = corner_value(s, table, l, f, bc, 1, 0, 1, 0);
+  const float c110 = corner_value(s, table, l, f, bc, 1, 1, 0, 0);
+  const float c111 = corner_value(s, table, l, f, bc, 1, 1, 1, 0);
+  const float ox = 1.0f - fx, oy = 1.0f - fy, oz = 1.0f - fz;
+  const float c00 = c000 * ox + c100 * fx;
+  const float c01 = c001 * ox + c101 * fx;
+  const float c10 = c010 * ox + c110 * fx;
+  const float c11 = c011 * ox + c111 * fx;
+  const float c0 = c00 * oy + c10 * fy;
+  const float c1 = c01 * oy + c11 * fy;
+  const float val = c0 * oz + c1 * fz;
+  g[0] = oz * (oy * (c100 - c000) + fy * (c110 - c010)) +
+         fz * (oy * (c101 - c001) + fy * (c111 - c011));
+  g[1] = oz * (ox * (c010 - c000) + fx * (c110 - c100)) +
+         fz * (ox * (c011 - c001) + fx * (c111 - c101));
+  g[2] = oy * (ox * (c001 - c000) + fx * (c101 - c100)) +
+         fy * (ox * (c011 - c010) + fx * (c111 - c110));
+  return val;
+}
+
+/* Partial derivatives of the quadrilinear interpolant (4D branch of
+ * emitGradientKernelImpl, mlp_kernel_emitter.cpp:1996-2024): each is a sum
+ * over the other three axes, loops nested in the order written there, of
+ * ((w_a*w_b)*w_c) * (upper - lower). */
+static void quadrilinear_grad(const tmo_spec *s, const float *table, int l,
+                              int f, const int32_t *bc, const float *fr,
+                              float *g) {
+  float c[2][2][2][2]; /* [dw][dz][dy][dx] */
+  for (int dw = 0; dw < 2; ++dw)
+    for (int dz = 0; dz < 2; ++dz)
+      for (int dy = 0; dy < 2; ++dy)
+        for (int dx = 0; dx < 2; ++dx)
+          c[dw][dz][dy][dx] = corner_value(s, table, l, f, bc, dx, dy, dz, dw);
+#define W_(a, k) ((k) == 0 ? 1.0f - fr[a] : fr[a])
+  float gx = 0, gy = 0, gz = 0, gt = 0;
+  for (int dw = 0; dw < 2; ++dw)
+    for (int dz = 0; dz < 2; ++dz)
+      for (int dy = 0; dy < 2; ++dy)
+        gx += ((W_(1, dy) * W_(2, dz)) * W_(3, dw)) *
+              (c[dw][dz][dy][1] - c[dw][dz][dy][0]);
+  for (int dw = 0; dw < 2; ++dw)
+    for (int dz = 0; dz < 2; ++dz)
+      for (int dx = 0; dx < 2; ++dx)
+        gy += ((W_(0, dx) * W_(2, dz)) * W_(3, dw)) *
+              (c[dw][dz][1][dx] - c[dw][dz][0][dx]);
+  for (int dw = 0; dw < 2; ++dw)
+    for (int dy = 0; dy < 2; ++dy)
+      for (int dx = 0; dx < 2; ++dx)
+        gz += ((W_(0, dx) * W_(1, dy)) * W_(3, dw)) *
+              (c[dw][1][dy][dx] - c[dw][0][dy][dx]);
+  for (int dz = 0; dz < 2; ++dz)
+    for (int dy = 0; dy < 2; ++dy)
+      for (int dx = 0; dx < 2; ++dx)
+        gt += ((W_(0, dx) * W_(1, dy)) * W_(2, dz)) *
+              (c[1][dz][dy][dx] - c[0][dz][dy][dx]);
+#undef W_
+  g[0] = gx; g[1] = gy; g[2] = gz; g[3] = gt;
+}
+
+static void cell_of(const tmo_spec *s, const float *p, float res, int32_t *bc,
+                    float *fr) {
+  for (int a = 0; a < s->d; ++a) {
+    const float sa = p[a] * res;
+    const float fl = floorf(sa);
+    bc[a] = (int32_t)fl;
+    fr[a] = sa - fl;
+  }
+}
+
+void tmo_eval_gradient(const tmo_spec *s, const float *table, const float *mlp,
+                       const float *pos, int64_t N, float *out, float *grad) {
+  float res[32];
+  offsets_t o;
+  tmo_level_resolutions(s, res);
+  mlp_offsets(s, &o);
+  const int W = s->W, F = s->F, H = s->H, d = s->d;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < N; ++i) {
+    const float *p = pos + i * d;
+    float acts[MAX_H][MAX_W], ga[MAX_W], gb[MAX_W];
+    int32_t bc[4];
+    float fr[4], tg[4];
+    /* forward (mlp_kernel_emitter.cpp:1892-1945): per level and feature the
+     * interpolated value times the W0 row, accumulated into h0 */
+    float *h0 = acts[0];
+    for (int j = 0; j < W; ++j) h0[j] = 0.0f;
+    for (int l = 0; l < s->L; ++l) {
+      cell_of(s, p, res[l], bc, fr);
+      for (int f = 0; f < F; ++f) {
+        float feat;
+        if (d == 4) {
+          corners_t c;
+          level_corners(s, p, res[l], l, &c);
+          feat = 0.0f;
+          for (int k = 0; k < c.n; ++k)
+            feat = feat + c.w[k] * table[c.off[k] + f];
+        } else {
+          feat = trilinear_grad(s, table, l, f, bc, fr, tg);
+        }
+        const float *wr = mlp + o.w_off[0] + (int64_t)(l * F + f) * W;
+        for (int j = 0; j < W; ++j) h0[j] = h0[j] + feat * wr[j];
+      }
+    }
+    for (int j = 0; j < W; ++j) {
+      const float t = h0[j] + mlp[o.b_off[0] + j];
+      h0[j] = t > 0.0f ? t : 0.0f;
+    }
+    for (int k = 1; k < H; ++k)
+      for (int j = 0; j < W; ++j) {
+        float acc = 0.0f;
+        for (int q = 0; q < W; ++q)
+          acc = acc + acts[k - 1][q] * mlp[o.w_off[k] + (int64_t)q * W + j];
+        const float t = acc + mlp[o.b_off[k] + j];
+        acts[k][j] = t > 0.0f ? t : 0.0f;
+      }
+    /* backward from d(out)/d(out) = 1 (:1947-1971): the output row masked by
+     * the last activation, then through the hidden layers */
+    float *cur = ga, *nxt = gb;
+    for (int j = 0; j < W; ++j)
+      cur[j] = mlp[o.w_off[H] + j] * (acts[H - 1][j] > 0.0f ? 1.0f : 0.0f);
+    for (int k = H - 1; k >= 1; --k) {
+      for (int q = 0; q < W; ++q) {
+        float acc = 0.0f;
+        for (int j = 0; j < W; ++j)
+          acc = acc + cur[j] * mlp[o.w_off[k] + (int64_t)q * W + j];
+        nxt[q] = acc * (acts[k - 1][q] > 0.0f ? 1.0f : 0.0f);
+      }
+      float *t = cur; cur = nxt; nxt = t;
+    }
+    /* position gradient (:1973-2033): sum over levels and features of
+     * (grad_feat * resolution) * d(interpolant)/d(frac) */
+    float gp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int l = 0; l < s->L; ++l) {
+      cell_of(s, p, res[l], bc, fr);
+      for (int f = 0; f < F; ++f) {
+        const float *wr = mlp + o.w_off[0] + (int64_t)(l * F + f) * W;
+        float gf = 0.0f;
+        for (int j = 0; j < W; ++j) gf = gf + cur[j] * wr[j];
+        if (d == 4)
+          quadrilinear_grad(s, table, l, f, bc, fr, tg);
+        else
+          trilinear_grad(s, table, l, f, bc, fr, tg);
+        const float sc = gf * res[l];
+        for (int a = 0; a < d; ++a) gp[a] = gp[a] + sc * tg[a];
+      }
+    }
+    /* output (:2064-2070): bias plus the last activations times the output
+     * column */
+    float y = mlp[o.b_off[H]];
+    for (int j = 0; j < W; ++j) y = y + acts[H - 1][j] * mlp[o.w_off[H] + j];
+    out[i] = y;
+    for (int a = 0; a < d; ++a) grad[i * d + a] = gp[a];
+  }
+}

@@ -69,6 +69,14 @@ void tmo_encode(const tmo_spec *s, const float *table, const float *pos,
 void tmo_forward(const tmo_spec *s, const float *table, const float *mlp,
                  const float *pos, int64_t N, float *out);
 
+/* Analytic input gradient of a single-output field (the EvalGradient kernel,
+ * mlp_kernel_emitter.cpp:1716-2090, scalar path): out [N] = the field value,
+ * grad [N x d] = d(out)/d(pos).  Requires O == 1.  The 3D value uses the
+ * lerp form of trilinear_feature_grad, so it can differ from tmo_forward by
+ * rounding. */
+void tmo_eval_gradient(const tmo_spec *s, const float *table, const float *mlp,
+                       const float *pos, int64_t N, float *out, float *grad);
+
 /* Plain MLP on given features x [N x L*F] (no encoding). */
 void tmo_mlp_forward(const tmo_spec *s, const float *mlp, const float *x,
                      int64_t N, float *out);

@@ -22,6 +22,8 @@ import ref_oracle  # noqa: E402
 
 N_POINTS = 300
 TAGS = ("ka", "sdf", "img", "d4", "f1", "f4", "cos")
+# single-output specs whose EvalGradient kernel output is also stored
+EVALGRAD_ONLY = ("d4o1", "h3")
 
 
 def case_inputs(tag, sp, seed=1):
@@ -46,6 +48,9 @@ def main():
         tr = ref_oracle.train(tag, sp, table, mlp, pos, tgt)
         ex = ref_oracle.train(tag, sp, table, mlp, pos, tgt, d_out=d_out)
         ev = ref_oracle.evaluate(tag, sp, table, mlp, pos)
+        extra = {}
+        if int(sp[6]) == 1:
+            extra["evalgrad"] = ref_oracle.eval_gradient(tag, sp, table, mlp, pos)
         nz = np.nonzero(tr["grad_hash"])[0].astype(np.uint32)
         nze = np.nonzero(ex["grad_hash"])[0].astype(np.uint32)
         np.savez_compressed(
@@ -53,7 +58,14 @@ def main():
             train_hash_idx=nz, train_hash_val=tr["grad_hash"][nz],
             train_mlp=tr["grad_mlp"], train_loss_sum=np.float64(tr["loss_partials"].sum()),
             train_mask=tr["mask"], ext_hash_idx=nze,
-            ext_hash_val=ex["grad_hash"][nze], ext_mlp=ex["grad_mlp"], eval=ev)
+            ext_hash_val=ex["grad_hash"][nze], ext_mlp=ex["grad_mlp"], eval=ev,
+            **extra)
+    for tag in EVALGRAD_ONLY:
+        sp = ref_oracle.spec_tuple(tag)
+        table, mlp, pos, _, _ = case_inputs(tag, sp)
+        np.savez_compressed(
+            os.path.join(HERE, f"ref_{tag}.npz"), spec=np.array(sp, np.float64),
+            evalgrad=ref_oracle.eval_gradient(tag, sp, table, mlp, pos))
     # Philox init, Morton codes, Adam: small vectors
     rng = np.random.default_rng(5)
     uni = ref_oracle.init_uniform(1027, -0.25, 0.75, 0xDEADBEEF12345678, 17)

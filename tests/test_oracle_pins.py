@@ -122,6 +122,50 @@ def test_eval_kernel_matches_reference_golden(tag):
     assert np.abs(out - g["eval"]).max() <= 1e-6 * max(1.0, np.abs(out).max())
 
 
+EVALGRAD_TAGS = ("ka", "sdf", "f1", "f4", "h3", "d4o1")
+
+
+@pytest.mark.parametrize("tag", EVALGRAD_TAGS)
+def test_eval_gradient_kernel_matches_reference_golden(tag):
+    """Reference EvalGradient kernel (mlp_kernel_emitter.cpp:1716-2090, scalar
+    path, resolution BASE*pow(SCALE, l)) vs the oracle: bit-exact.  The
+    kernel writes [value, d/dx, d/dy, d/dz]; in 4D the d/dw component is not
+    written, so only the first three are compared."""
+    g = np.load(os.path.join(GOLDEN, f"ref_{tag}.npz"))
+    sp = tuple(g["spec"])
+    table, mlp, pos, _, _ = case_inputs(tag, sp)
+    out, grad = o.eval_gradient(spec_from(sp, res_mode=1), table, mlp, pos)
+    ref = g["evalgrad"]
+    assert np.array_equal(out, ref[:, 0])
+    assert np.array_equal(grad[:, :3], ref[:, 1:4])
+
+
+def test_eval_gradient_matches_finite_differences():
+    """d(value)/d(pos) agrees with central differences of the oracle's own
+    value (known-answer style rule of test_default_trainer.cpp:2338-2412),
+    away from cell boundaries."""
+    sp = (4, 2, 10, 3, 16, 2, 1, 0, 4.0, 1.5, 1.0)
+    s = spec_from(sp, res_mode=0)
+    table, mlp, pos, _, _ = case_inputs("fd", sp, seed=7)
+    pos = pos[:64].astype(np.float64)
+    _, grad = o.eval_gradient(s, table, mlp, pos.astype(np.float32))
+    h = 1e-3
+    ok = 0
+    for i in range(pos.shape[0]):
+        for a in range(3):
+            pp, pm = pos[i].copy(), pos[i].copy()
+            pp[a] += h
+            pm[a] -= h
+            vp, _ = o.eval_gradient(s, table, mlp, pp[None].astype(np.float32))
+            vm, _ = o.eval_gradient(s, table, mlp, pm[None].astype(np.float32))
+            fd = (float(vp[0]) - float(vm[0])) / (2 * h)
+            if abs(fd - grad[i, a]) <= 2e-2 * max(1.0, abs(fd)):
+                ok += 1
+    # points whose +-h stencil crosses a cell face of some level or a ReLU
+    # kink do not follow the local derivative; they are a small minority
+    assert ok >= 0.9 * pos.shape[0] * 3
+
+
 def test_static_kernels_match_reference_golden():
     g = np.load(os.path.join(GOLDEN, "ref_static.npz"))
     assert np.array_equal(o.init_uniform(1027, -0.25, 0.75, 0xDEADBEEF12345678, 17),

@@ -21,6 +21,12 @@ void launch_forward_exact(const NetDims &nd, const float *table,
                           const float *mlp, const float *pos, float *out,
                           uint32_t N, float *scratch, int num_sms,
                           cudaStream_t st);
+size_t eval_gradient_scratch_floats(const NetDims &nd, int num_sms);
+// Value [N] and d(value)/d(pos) [N x d] of a single-output field.
+void launch_eval_gradient(const NetDims &nd, const float *table,
+                          const float *mlp, const float *pos, float *out,
+                          float *grad, uint32_t N, float *scratch, int num_sms,
+                          cudaStream_t st);
 void launch_encode_debug(const NetDims &nd, const float *table,
                          const float *pos, float *feat, uint32_t *corner_idx,
                          int32_t *cells, uint32_t N, cudaStream_t st);

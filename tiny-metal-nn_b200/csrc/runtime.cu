@@ -114,6 +114,7 @@ struct tmnn_ctx {
   DevBuf<float> scratch;
   // batch staging
   DevBuf<float> pos_in, tgt_in, pos_s, tgt_s, out_buf, out_s;
+  DevBuf<float> grad_out, eg_scratch;  // evaluate_with_gradient
   DevBuf<uint32_t> codes, codes_alt, idx, perm;
   DevBuf<uint8_t> sort_tmp;
   double *h_loss = nullptr;  // pinned
@@ -743,6 +744,45 @@ void forward_api(tmnn_ctx &c, const float *pos, float *out, uint32_t N,
   CK(cudaGetLastError());
 }
 
+// FieldEvaluator::evaluate_with_gradient (default_trainer.cpp:467-622): the
+// field value [N] and d(value)/d(pos) [N x d] of a single-output network, from
+// the fp32 parameters (the reference compiles this kernel with fp16 off).
+void evaluate_with_gradient(tmnn_ctx &c, const float *pos, float *out,
+                            float *grad, uint32_t N, uint32_t flags) {
+  if (c.nd.O != 1)
+    throw std::invalid_argument(
+        "evaluate_with_gradient: the network must have exactly one output "
+        "(num_outputs = " + std::to_string(c.nd.O) + ")");
+  if (N > 0 && (!pos || !out || !grad))
+    throw std::invalid_argument(
+        "evaluate_with_gradient: positions, output, and gradients must be "
+        "non-null when N > 0");
+  require_synced(c, "evaluate_with_gradient");
+  if (N == 0) return;
+  CK(cudaSetDevice(c.device));
+  ensure_batch(c, N);
+  const size_t d = c.nd.d;
+  const float *p = stage_in(c, pos, (size_t)N * d, c.pos_in, flags);
+  const bool dev = flags & TMNN_PTR_DEVICE;
+  float *o = dev ? out : c.out_buf.p;
+  float *g = grad;
+  if (!dev) {
+    c.grad_out.ensure((size_t)N * d);
+    g = c.grad_out.p;
+  }
+  const size_t sf = eval_gradient_scratch_floats(c.nd, c.num_sms);
+  if (sf) c.eg_scratch.ensure(sf);
+  launch_eval_gradient(c.nd, c.hash_w(), c.mlp_w(), p, o, g, N,
+                       c.eg_scratch.p, c.num_sms, c.stream);
+  c.launches++;
+  if (!dev) {
+    copy_out(c, out, o, N, flags);
+    copy_out(c, grad, g, (size_t)N * d, flags);
+  }
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+}
+
 void backward_accumulate(tmnn_ctx &c, const float *pos, const float *dout,
                          uint32_t N, uint32_t flags) {
   if (N > 0 && (!pos || !dout))
@@ -1087,6 +1127,17 @@ tmnn_status tmnn_cuda_evaluate(tmnn_ctx *c, const float *positions,
   return guarded([&] {
     BusyGuard g(c);
     forward_api(*c, positions, outputs, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_evaluate_with_gradient(tmnn_ctx *c,
+                                             const float *positions,
+                                             float *outputs, float *gradients,
+                                             uint32_t n, uint32_t flags) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    evaluate_with_gradient(*c, positions, outputs, gradients, n, flags);
   });
 }
 

@@ -315,6 +315,35 @@ class Trainer:
 
     evaluate = inference
 
+    def evaluate_with_gradient(self, input, out=None, gradients=None):
+        """(values [N, 1], gradients [N, n_input]) of a single-output field:
+        the value and d(value)/d(position) (Trainer::evaluate_with_gradient,
+        trainer.h:378-386).  Host arrays or CUDA tensors, like inference()."""
+        h = self._handle()
+        pp, n, flags, _k = _arg(input, "input", self.n_input)
+        if flags & _abi.PTR_DEVICE:
+            import torch
+            if out is None:
+                out = torch.empty((n, self.n_output), dtype=torch.float32,
+                                  device=input.device)
+            if gradients is None:
+                gradients = torch.empty((n, self.n_input), dtype=torch.float32,
+                                        device=input.device)
+            optr = C.c_void_p(out.data_ptr())
+            gptr = C.c_void_p(gradients.data_ptr())
+        else:
+            if out is None:
+                out = np.empty((n, self.n_output), np.float32)
+            if gradients is None:
+                gradients = np.empty((n, self.n_input), np.float32)
+            optr = out.ctypes.data_as(C.c_void_p)
+            gptr = gradients.ctypes.data_as(C.c_void_p)
+        self._guarded(lambda: _check(lib.tmnn_cuda_evaluate_with_gradient(
+            h, pp, optr, gptr, n, flags), "evaluate_with_gradient"))
+        return out, gradients
+
+    inference_with_gradient = evaluate_with_gradient
+
     def debug_encode(self, input):
         """(features, corner_index, cells) of the encoding (host arrays)."""
         h = self._handle()

@@ -99,6 +99,7 @@ _SIGS = [
     ("tmnn_cuda_backward_accumulate", C.c_int, [P, P, P, u32, u32]),
     ("tmnn_cuda_adam_step", C.c_int, [P]),
     ("tmnn_cuda_evaluate", C.c_int, [P, P, P, u32, u32]),
+    ("tmnn_cuda_evaluate_with_gradient", C.c_int, [P, P, P, P, u32, u32]),
     ("tmnn_cuda_debug_encode", C.c_int, [P, P, u32, P, P, P]),
     ("tmnn_cuda_export_opt_state", C.c_int,
      [P, P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(u32)]),
