@@ -52,9 +52,11 @@ WORKLOADS = {
                          "T=2^22, MLP 64x2 -> 4, L2, Adam lr 1e-2"),
 }
 
-# DRAM bytes per fwd/bwd launch from the committed ncu capture of the
-# dominant kernel (profiles/), per workload and family; None until captured.
-NCU_TRAFFIC_PER_SAMPLE = {}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample of the
+# dominant kernel, from the committed ncu capture of the same bench command
+# (profiles/fused_train_sdf3d.md: 162.2 MB per 2^18-point launch), per
+# workload and family; absent pairs report traffic null.
+NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 162.2e6 / (1 << 18)}
 
 
 def log(*a):
@@ -481,7 +483,8 @@ def main():
                      "unit": "GB/s", "frac": achieved / hbm,
                      "peak_source": peak_note,
                      "algorithmic_bytes_per_sample": per_sample,
-                     "traffic": None if traffic is None else traffic * B},
+                     "traffic": None if traffic is None else traffic * B,
+                     "traffic_unit": "bytes per launch (ncu)"},
         "roofline_adam": {"bound": "hbm",
                           "achieved": adam_bytes / (statistics.mean(ad) / 1e3) / 1e9,
                           "peak": hbm, "unit": "GB/s",
