@@ -119,8 +119,39 @@ typedef struct tmnn_train_cfg {
                                       ranks on, Adam is sharded over the
                                       ranks (reduce-scatter, Adam on 1/world
                                       of the table, all-gather) */
-  int32_t reserved[6];
+  /* numerics guard (RuntimePolicy, include/tiny-metal-nn/runtime_policy.h:
+   * 13-40; defaults from TMNN_NUMERICS_SAMPLING_MODE,
+   * TMNN_NUMERICS_SAMPLE_INTERVAL, TMNN_BAD_STEP_MODE like
+   * load_runtime_policy, src/tiny_metal_nn/runtime/runtime_policy.h:144-175) */
+  int32_t numerics_sampling_mode; /* tmnn_numerics_sampling */
+  int32_t numerics_sample_interval; /* steps between sampled probes (128) */
+  int32_t bad_step_recovery;      /* tmnn_bad_step_recovery */
+  int32_t reserved[3];
 } tmnn_train_cfg;
+
+/* NumericsSamplingMode (runtime_policy.h:13-18). */
+typedef enum tmnn_numerics_sampling {
+  TMNN_NUMERICS_SAMPLED = 0,   /* steps 0 and 1, every interval, after an anomaly */
+  TMNN_NUMERICS_PERIODIC = 1,  /* every interval, after an anomaly */
+  TMNN_NUMERICS_FULL = 2,      /* every step */
+  TMNN_NUMERICS_DISABLED = 3   /* only when the loss is not finite */
+} tmnn_numerics_sampling;
+
+/* BadStepRecoveryMode (runtime_policy.h:20-26) and BadStepRecoveryAction
+ * (include/tiny-metal-nn/common.h:71-76). */
+typedef enum tmnn_bad_step_recovery {
+  TMNN_BAD_STEP_SIGNAL_ONLY = 0,
+  TMNN_BAD_STEP_THROW = 1,
+  TMNN_BAD_STEP_SKIP = 2,
+  TMNN_BAD_STEP_ROLLBACK = 3,
+  TMNN_BAD_STEP_SAFE_FAMILY_RETRY = 4
+} tmnn_bad_step_recovery;
+typedef enum tmnn_recovery_action {
+  TMNN_RECOVERY_NONE = 0,
+  TMNN_RECOVERY_SKIPPED = 1,
+  TMNN_RECOVERY_ROLLED_BACK = 2,
+  TMNN_RECOVERY_RETRIED_WITH_SAFE_FAMILY = 3
+} tmnn_recovery_action;
 
 /* TrainingStepResult (include/tiny-metal-nn/common.h:97-110), reduced. */
 typedef struct tmnn_step_result {
@@ -134,7 +165,28 @@ typedef struct tmnn_step_result {
   float fwd_bwd_ms;    /* device time of forward/backward/scatter */
   float allreduce_ms;  /* device time of the gradient allreduce */
   float adam_ms;       /* device time of Adam + gradient reset */
+  /* NumericsReport (include/tiny-metal-nn/detail/runtime_stats.h:32-40) of
+   * the step, from the device probe; backward/update fields are meaningful
+   * when numerics_probed is 1 */
+  float grad_norm;            /* sqrt(sum g^2) over finite gradients */
+  int32_t finite_forward;
+  int32_t finite_backward;
+  int32_t finite_update;
+  float max_abs_gradient;
+  float max_abs_update;
+  int32_t numerics_probed;    /* the probe scanned this step's gradients */
+  int32_t numerics_reported;  /* the guard recorded this step */
+  int32_t has_numerics_anomaly;
+  int32_t recovery_action;    /* tmnn_recovery_action */
 } tmnn_step_result;
+
+/* Counters of the numerics guard (context_record_training_step,
+ * training_step_execution.cpp:1047-1058). */
+typedef struct tmnn_numerics_stats {
+  uint64_t reports, anomalies, skipped, rolled_back, safe_family_recoveries;
+  uint32_t last_anomaly_step;
+  int32_t safe_family_active; /* 1 after a FallbackAndRetry switched family */
+} tmnn_numerics_stats;
 
 /* RuntimeBufferRole (include/tiny-metal-nn/detail/runtime_authority.h:68-79) */
 typedef enum tmnn_buffer_role {
@@ -268,6 +320,10 @@ tmnn_status tmnn_cuda_evaluate_with_gradient(tmnn_ctx *ctx,
                                              const float *positions,
                                              float *outputs, float *gradients,
                                              uint32_t n, uint32_t flags);
+
+/* Numerics guard counters of this context. */
+tmnn_status tmnn_cuda_get_numerics_stats(tmnn_ctx *ctx,
+                                         tmnn_numerics_stats *out);
 
 /* Encoding only (parity instrument): features [n x L*F] f32, and when
  * non-NULL the first table index of every corner [n x L x 2^d] (u32) and the

@@ -49,6 +49,31 @@ def test_default_config_matches_reference_defaults():
     assert c.seed == 42 and abs(c.hash_init_range - 1e-4) < 1e-10
 
 
+@pytest.mark.parametrize("env,field,value", [
+    ({"TMNN_BAD_STEP_MODE": " Skip "}, "bad_step_recovery", 2),
+    ({"TMNN_BAD_STEP_MODE": "safe-family-fallback"}, "bad_step_recovery", 4),
+    ({"TMNN_BAD_STEP_MODE": "strict"}, "bad_step_recovery", 1),
+    ({"TMNN_NUMERICS_SAMPLING_MODE": "full-per-step"}, "numerics_sampling_mode", 2),
+    ({"TMNN_NUMERICS_SAMPLING_MODE": "OFF"}, "numerics_sampling_mode", 3),
+    ({"TMNN_NUMERICS_SAMPLE_INTERVAL": "0"}, "numerics_sample_interval", 1),
+    ({"TMNN_NUMERICS_SAMPLE_INTERVAL": "32"}, "numerics_sample_interval", 32),
+    ({}, "numerics_sample_interval", 128),
+])
+def test_numerics_policy_from_environment(monkeypatch, env, field, value):
+    """load_runtime_policy's environment variables and spellings
+    (src/tiny_metal_nn/runtime/runtime_policy.h:78-161)."""
+    import tmnn_b200 as t
+    from tmnn_b200 import _abi
+    for k in ("TMNN_BAD_STEP_MODE", "TMNN_NUMERICS_SAMPLING_MODE",
+              "TMNN_NUMERICS_SAMPLE_INTERVAL"):
+        monkeypatch.delenv(k, raising=False)
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    c = _abi.TrainCfg()
+    t.lib.tmnn_cuda_default_train_cfg(C.byref(c))
+    assert getattr(c, field) == value
+
+
 def _create(cfg_json, n_in=3, n_out=1):
     import tmnn_b200 as t
     h = C.c_void_p()
@@ -69,6 +94,8 @@ def _create(cfg_json, n_in=3, n_out=1):
     ('{"bogus": 1}', "config.bogus: unknown key"),
     ('{"encoding": {"n_levels": 2.5}}', "must be an integer"),
     ('{"encoding": ', "json:"),
+    ('{"b200": {"bad_step_recovery": "Retry"}}', "allowed: SignalOnly, Throw"),
+    ('{"b200": {"numerics_sampling_mode": "Often"}}', "allowed: Sampled"),
 ])
 def test_config_errors_reported_without_gpu(cfg, frag):
     st, msg, _ = _create(cfg)

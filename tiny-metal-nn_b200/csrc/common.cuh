@@ -65,6 +65,20 @@ __device__ inline int32_t fixed_trunc(float x) {
   return (int32_t)x;
 }
 
+// Per-step device statistics: the summed loss (written by the forward/backward
+// kernels) followed by the numerics probe's results.  One memset clears it,
+// one copy reads it back.
+struct StepStats {
+  double loss;            // sum of per-point losses
+  double grad_l2;         // sum of squared finite gradients
+  float max_abs_grad;     // max |g| over finite gradients
+  float max_abs_update;   // max |w - w'| of the would-be Adam update
+  float nonfinite_bwd;    // 1 when a gradient is NaN/Inf
+  float nonfinite_upd;    // 1 when a would-be update quantity is NaN/Inf
+  int32_t probed;         // 1 when the probe scanned the gradients
+  int32_t gate;           // 1: Adam skips the update on an anomaly
+};
+
 struct AdamArgs {
   float lr_hash, lr_mlp, beta1, beta2, eps, bc1, bc2, l1_hash, l2_mlp,
       grad_clip, weight_decay;
@@ -75,6 +89,16 @@ struct AdamArgs {
   int32_t sparse;       // update only touched hash slots
   int32_t grad_fixed;
   int32_t implicit_touch;  // touched = byte set or nonzero float gradient
+  const StepStats *guard;  // non-null: skip the update when the gated probe
+                           // found an anomaly (gradients are still cleared)
 };
+
+// Whether the numerics guard vetoes this step's update.
+__device__ inline bool adam_vetoed(const AdamArgs &a) {
+  if (!a.guard || !a.guard->gate) return false;
+  const double l = a.guard->loss;
+  return a.guard->nonfinite_bwd != 0.0f || a.guard->nonfinite_upd != 0.0f ||
+         !(l - l == 0.0);
+}
 
 }  // namespace tmnn

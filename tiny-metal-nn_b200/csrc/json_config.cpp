@@ -387,7 +387,8 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
   // this build's execution knobs
   const JVal &b2 = section("b200");
   known_keys(b2, {"family", "hash_grad_format", "table_dtype", "morton_sort",
-                  "sparse_hash_adam", "active_levels"},
+                  "sparse_hash_adam", "active_levels", "numerics_sampling_mode",
+                  "numerics_sample_interval", "bad_step_recovery"},
              "b200", d);
   const std::string fam = str(b2, "family", "Auto", "b200.family", d);
   if (fam == "Auto") cfg->family = TMNN_FAMILY_AUTO;
@@ -411,6 +412,38 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
     cfg->sparse_hash_adam =
         boolean(b2, "sparse_hash_adam", true, "b200.sparse_hash_adam", d) ? 1 : 0;
   cfg->active_levels = integer(b2, "active_levels", 0, "b200.active_levels", d);
+  // RuntimePolicyOverrides (include/tiny-metal-nn/runtime_policy.h:43-52):
+  // the numerics guard knobs, with the enum names of the reference
+  if (b2.get("numerics_sampling_mode")) {
+    const std::string m = str(b2, "numerics_sampling_mode", "Sampled",
+                              "b200.numerics_sampling_mode", d);
+    if (m == "Sampled") cfg->numerics_sampling_mode = TMNN_NUMERICS_SAMPLED;
+    else if (m == "Periodic") cfg->numerics_sampling_mode = TMNN_NUMERICS_PERIODIC;
+    else if (m == "FullPerStep") cfg->numerics_sampling_mode = TMNN_NUMERICS_FULL;
+    else if (m == "Disabled") cfg->numerics_sampling_mode = TMNN_NUMERICS_DISABLED;
+    else d.err("b200.numerics_sampling_mode",
+               "unsupported value '" + m +
+                   "'; allowed: Sampled, Periodic, FullPerStep, Disabled");
+  }
+  if (b2.get("numerics_sample_interval")) {
+    const int n = integer(b2, "numerics_sample_interval", 128,
+                          "b200.numerics_sample_interval", d);
+    cfg->numerics_sample_interval = n > 0 ? n : 1;
+  }
+  if (b2.get("bad_step_recovery")) {
+    const std::string m = str(b2, "bad_step_recovery", "SignalOnly",
+                              "b200.bad_step_recovery", d);
+    if (m == "SignalOnly") cfg->bad_step_recovery = TMNN_BAD_STEP_SIGNAL_ONLY;
+    else if (m == "Throw") cfg->bad_step_recovery = TMNN_BAD_STEP_THROW;
+    else if (m == "Skip") cfg->bad_step_recovery = TMNN_BAD_STEP_SKIP;
+    else if (m == "Rollback") cfg->bad_step_recovery = TMNN_BAD_STEP_ROLLBACK;
+    else if (m == "FallbackAndRetryWithSafeFamily")
+      cfg->bad_step_recovery = TMNN_BAD_STEP_SAFE_FAMILY_RETRY;
+    else d.err("b200.bad_step_recovery",
+               "unsupported value '" + m +
+                   "'; allowed: SignalOnly, Throw, Skip, Rollback, "
+                   "FallbackAndRetryWithSafeFamily");
+  }
 
   if (!d.errors.empty()) {
     std::string msg = "create_from_config: ";

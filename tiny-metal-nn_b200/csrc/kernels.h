@@ -34,6 +34,13 @@ void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
                  int32_t *gh_fixed, float *gh_float, float *gm,
                  uint8_t *touched, __half *table_h, int num_sms,
                  cudaStream_t st);
+// Numerics probe over [hash (a.hash_count from w/m/v/grads) | mlp (gm; w, m,
+// v at mlp_base)] into st; see kernels_exact.cu.
+void launch_numerics_probe(const AdamArgs &a, const float *w, const float *m,
+                           const float *v, const int32_t *gh_fixed,
+                           const float *gh_float, const float *gm,
+                           uint64_t mlp_base, StepStats *st, int force,
+                           int gate, int num_sms, cudaStream_t st_);
 void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
                                int entry_width, int num_sms, cudaStream_t st);
 void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,

@@ -401,6 +401,7 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
                        float *gh_float, float *__restrict__ gm,
                        uint8_t *__restrict__ touched, __half *table_h) {
   const uint64_t total = a.slots + a.mlp_count;
+  const bool veto = adam_vetoed(a);
   for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
        t += (uint64_t)gridDim.x * blockDim.x) {
     if (t < a.slots) {
@@ -416,7 +417,7 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
           g = gh_float[e];
           gh_float[e] = 0.0f;
         }
-        if (!on) continue;
+        if (!on || veto) continue;
         float wv = w[e], mv = m[e], vv = v[e];
         adam_elem(wv, mv, vv, g, a.lr_hash, a, a.l1_hash, false);
         w[e] = wv;
@@ -429,6 +430,7 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
       const uint64_t e = a.hash_count + j;
       const float g = gm[j];
       gm[j] = 0.0f;
+      if (veto) continue;
       float wv = w[e], mv = m[e], vv = v[e];
       adam_elem(wv, mv, vv, g, a.lr_mlp, a, a.l2_mlp, true);
       w[e] = wv;
@@ -446,6 +448,23 @@ __global__ void __launch_bounds__(256)
                  float *__restrict__ v, int32_t *gh_fixed, float *gh_float,
                  uint8_t *__restrict__ touched, __half *table_h) {
   const uint64_t n4 = a.hash_count / 4;
+  if (adam_vetoed(a)) {
+    // the numerics guard rejected the step: only reset gradients and marks
+    for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+         q += (uint64_t)gridDim.x * blockDim.x) {
+      if (a.sparse) {
+        if (a.entry_width == 2)
+          reinterpret_cast<uchar2 *>(touched)[q] = make_uchar2(0, 0);
+        else
+          reinterpret_cast<uchar4 *>(touched)[q] = make_uchar4(0, 0, 0, 0);
+      }
+      if (a.grad_fixed)
+        reinterpret_cast<int4 *>(gh_fixed)[q] = make_int4(0, 0, 0, 0);
+      else
+        reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    return;
+  }
   for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
        q += (uint64_t)gridDim.x * blockDim.x) {
     bool on[4] = {true, true, true, true};
@@ -508,6 +527,129 @@ __global__ void __launch_bounds__(256)
       reinterpret_cast<uint2 *>(table_h)[q] = *reinterpret_cast<uint2 *>(h);
     }
   }
+}
+
+// ------------------------------------------------------------ numerics probe
+
+// The reference's sampled numerics probes (training_step_execution.cpp:
+// 237-250 probe_backward_numerics, :290-340 accumulate_update_probe_for_range)
+// evaluated on the device over the gradients before Adam: finiteness, max
+// |g| and sum g^2 of the finite gradients; and, per element, the Adam update
+// the step would apply (same arithmetic as the probe: clip, decay or L1/L2,
+// moments, bias corrections, candidate weight), its finiteness and max
+// |w - w'|.  Every parameter is scanned (dense), as the reference does.
+// Unless `force`, the probe returns at once when the step's loss is finite,
+// so launching it every step costs one empty launch.
+__device__ inline void atomic_max_nonneg(float *p, float v) {
+  atomicMax(reinterpret_cast<int *>(p), __float_as_int(v));
+}
+
+__device__ inline bool probe_elem(float g, float w, float m, float v, float lr,
+                                  float reg, bool is_mlp, const AdamArgs &a,
+                                  float &du) {
+  if (a.grad_clip > 0.0f)
+    g = g < -a.grad_clip ? -a.grad_clip : (g > a.grad_clip ? a.grad_clip : g);
+  if (a.weight_decay > 0.0f) {
+  } else if (!is_mlp && reg > 0.0f) {
+    g = g + reg * (w > 0.0f ? 1.0f : (w < 0.0f ? -1.0f : 0.0f));
+  } else if (is_mlp && reg > 0.0f) {
+    g = g + reg * w;
+  }
+  const float mn = a.beta1 * m + (1.0f - a.beta1) * g;
+  const float vn = a.beta2 * v + ((1.0f - a.beta2) * g) * g;
+  const float mh = mn / a.bc1;
+  const float vh = vn / a.bc2;
+  const float ad = (lr * mh) / (sqrtf(vh) + a.eps);
+  const float wd = a.weight_decay > 0.0f ? (lr * a.weight_decay) * w : 0.0f;
+  const float cand = (w - wd) - ad;
+  du = w - cand;
+  return isfinite(g) && isfinite(mn) && isfinite(vn) && isfinite(mh) &&
+         isfinite(vh) && isfinite(ad) && isfinite(wd) && isfinite(cand) &&
+         isfinite(du);
+}
+
+__global__ void __launch_bounds__(256)
+    k_numerics_probe(AdamArgs a, const float *__restrict__ w,
+                     const float *__restrict__ m, const float *__restrict__ v,
+                     const int32_t *__restrict__ gh_fixed,
+                     const float *__restrict__ gh_float,
+                     const float *__restrict__ gm, uint64_t mlp_base,
+                     StepStats *st, int force, int gate) {
+  const double loss = st->loss;
+  if (!force && loss - loss == 0.0) return;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    st->probed = 1;
+    st->gate = gate;
+  }
+  const uint64_t total = a.hash_count + a.mlp_count;
+  double l2 = 0.0;
+  float mg = 0.0f, mu = 0.0f;
+  bool bad_g = false, bad_u = false;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const bool is_mlp = i >= a.hash_count;
+    const uint64_t e = is_mlp ? mlp_base + (i - a.hash_count) : i;
+    float g;
+    if (is_mlp)
+      g = gm[i - a.hash_count];
+    else
+      g = a.grad_fixed ? (float)gh_fixed[i] * kInvGradScale : gh_float[i];
+    if (!isfinite(g)) {
+      bad_g = true;
+      continue;
+    }
+    mg = fmaxf(mg, fabsf(g));
+    l2 += (double)g * (double)g;
+    float du;
+    if (probe_elem(g, w[e], m[e], v[e], is_mlp ? a.lr_mlp : a.lr_hash,
+                   is_mlp ? a.l2_mlp : a.l1_hash, is_mlp, a, du))
+      mu = fmaxf(mu, fabsf(du));
+    else
+      bad_u = true;
+  }
+  __shared__ double s_l2[8];
+  __shared__ float s_mg[8], s_mu[8];
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  for (int o = 16; o > 0; o >>= 1) {
+    l2 += __shfl_down_sync(0xffffffffu, l2, o);
+    mg = fmaxf(mg, __shfl_down_sync(0xffffffffu, mg, o));
+    mu = fmaxf(mu, __shfl_down_sync(0xffffffffu, mu, o));
+  }
+  __syncthreads();
+  if (bad_g) atomicOr(&s_bad, 1);
+  if (bad_u) atomicOr(&s_bad, 2);
+  const int wid = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    s_l2[wid] = l2;
+    s_mg[wid] = mg;
+    s_mu[wid] = mu;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int k = 1; k < (int)(blockDim.x >> 5); ++k) {
+      l2 += s_l2[k];
+      mg = fmaxf(mg, s_mg[k]);
+      mu = fmaxf(mu, s_mu[k]);
+    }
+    if (l2 != 0.0) atomicAdd(&st->grad_l2, l2);
+    atomic_max_nonneg(&st->max_abs_grad, mg);
+    atomic_max_nonneg(&st->max_abs_update, mu);
+    if (s_bad & 1) st->nonfinite_bwd = 1.0f;
+    if (s_bad & 2) st->nonfinite_upd = 1.0f;
+  }
+}
+
+void launch_numerics_probe(const AdamArgs &a, const float *w, const float *m,
+                           const float *v, const int32_t *gh_fixed,
+                           const float *gh_float, const float *gm,
+                           uint64_t mlp_base, StepStats *st, int force,
+                           int gate, int num_sms, cudaStream_t st_) {
+  // unforced: one block checks the loss and scans only when it is not
+  // finite (rare, and then slow is fine); forced: the whole device
+  k_numerics_probe<<<force ? num_sms * 8 : 1, 256, 0, st_>>>(a, w, m, v, gh_fixed,
+                                                 gh_float, gm, mlp_base, st,
+                                                 force, gate);
 }
 
 // Completes the touched map of the implicit-touch mode: a slot whose float

@@ -10,6 +10,8 @@
 #include <nccl.h>
 
 #include <atomic>
+#include <cctype>
+#include <cstdlib>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -34,6 +36,9 @@ struct CapacityError : std::runtime_error {
   using std::runtime_error::runtime_error;
 };
 struct ConcurrentCall : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct OperationFailed : std::runtime_error {
   using std::runtime_error::runtime_error;
 };
 
@@ -81,6 +86,38 @@ struct DevBuf {
   size_t bytes() const { return n * sizeof(T); }
 };
 
+// NumericsGuard (src/tiny_metal_nn/runtime/numerics_guard.cpp:12-48): which
+// steps the probe records, and the anomaly bookkeeping.
+struct NumericsGuard {
+  int mode = TMNN_NUMERICS_SAMPLED;
+  uint32_t interval = 128;
+  uint32_t anomaly_count = 0, last_anomaly_step = 0;
+  uint64_t report_count = 0;
+  bool should_sample(uint32_t step, bool force) const {
+    if (force) return true;
+    switch (mode) {
+      case TMNN_NUMERICS_DISABLED:
+        return false;
+      case TMNN_NUMERICS_FULL:
+        return true;
+      case TMNN_NUMERICS_PERIODIC:
+        if (anomaly_count > 0 && step == last_anomaly_step + 1) return true;
+        return step != 0 && step % interval == 0;
+      default:
+        if (step == 0 || step == 1) return true;
+        if (anomaly_count > 0 && step == last_anomaly_step + 1) return true;
+        return step % interval == 0;
+    }
+  }
+  void record(uint32_t step, bool anomaly) {
+    ++report_count;
+    if (anomaly) {
+      ++anomaly_count;
+      last_anomaly_step = step;
+    }
+  }
+};
+
 }  // namespace
 
 struct tmnn_ctx {
@@ -110,14 +147,20 @@ struct tmnn_ctx {
   DevBuf<int32_t> gh_fixed;
   DevBuf<float> gh_float, gm;
   DevBuf<uint8_t> touched;
-  DevBuf<double> loss_acc;
+  DevBuf<double> loss_acc;  // a StepStats (loss first), see stats()
   DevBuf<float> scratch;
   // batch staging
   DevBuf<float> pos_in, tgt_in, pos_s, tgt_s, out_buf, out_s;
   DevBuf<float> grad_out, eg_scratch;  // evaluate_with_gradient
   DevBuf<uint32_t> codes, codes_alt, idx, perm;
   DevBuf<uint8_t> sort_tmp;
-  double *h_loss = nullptr;  // pinned
+  StepStats *h_stats = nullptr;  // pinned copy of the step statistics
+  double *h_loss = nullptr;      // &h_stats->loss
+  // numerics guard
+  NumericsGuard guard;
+  uint64_t n_skipped = 0, n_rolled_back = 0, n_safe_recoveries = 0;
+  bool safe_family_active = false;
+  StepStats *stats() { return reinterpret_cast<StepStats *>(loss_acc.p); }
   cudaEvent_t ev[6] = {};
   FusedWorkspace fws;
   // data parallelism
@@ -135,7 +178,7 @@ struct tmnn_ctx {
   ~tmnn_ctx() {
     if (stream) cudaStreamSynchronize(stream);
     if (comm) ncclCommDestroy(comm);
-    if (h_loss) cudaFreeHost(h_loss);
+    if (h_stats) cudaFreeHost(h_stats);
     for (auto e : ev)
       if (e) cudaEventDestroy(e);
     fused_release(fws);
@@ -186,6 +229,65 @@ tmnn_status guarded(F &&f) {
     g_last_error = "null context"; \
     return TMNN_ERR_NULL_OBJECT;   \
   }
+
+// The numerics-policy environment variables of load_runtime_policy
+// (src/tiny_metal_nn/runtime/runtime_policy.h:78-140, :155-161), same
+// spellings; an unknown value leaves the default (the reference throws from
+// its constructor; here defaults are filled by a function that cannot fail).
+bool env_is(const char *v, const char *a) {
+  for (; *v && *a; ++v, ++a)
+    if (std::tolower((unsigned char)*v) != std::tolower((unsigned char)*a))
+      return false;
+  return *v == 0 && *a == 0;
+}
+
+std::string env_trim(const char *name) {
+  const char *v = std::getenv(name);
+  if (!v) return {};
+  std::string s(v);
+  const size_t b = s.find_first_not_of(" \t\n\r");
+  const size_t e = s.find_last_not_of(" \t\n\r");
+  return b == std::string::npos ? std::string() : s.substr(b, e - b + 1);
+}
+
+void apply_policy_env(tmnn_train_cfg &c) {
+  std::string v = env_trim("TMNN_NUMERICS_SAMPLING_MODE");
+  if (!v.empty()) {
+    const char *x = v.c_str();
+    if (env_is(x, "sampled") || env_is(x, "default"))
+      c.numerics_sampling_mode = TMNN_NUMERICS_SAMPLED;
+    else if (env_is(x, "periodic") || env_is(x, "steady-state") ||
+             env_is(x, "interval-only"))
+      c.numerics_sampling_mode = TMNN_NUMERICS_PERIODIC;
+    else if (env_is(x, "full") || env_is(x, "full-per-step"))
+      c.numerics_sampling_mode = TMNN_NUMERICS_FULL;
+    else if (env_is(x, "disabled") || env_is(x, "off"))
+      c.numerics_sampling_mode = TMNN_NUMERICS_DISABLED;
+  }
+  v = env_trim("TMNN_NUMERICS_SAMPLE_INTERVAL");
+  if (!v.empty()) {
+    char *end = nullptr;
+    const unsigned long n = std::strtoul(v.c_str(), &end, 10);
+    if (end != v.c_str() && *end == 0 && n <= 0xFFFFFFFFul)
+      c.numerics_sample_interval = (int32_t)(n > 0 ? (n > 0x7FFFFFFF ? 0x7FFFFFFF : n) : 1);
+  }
+  v = env_trim("TMNN_BAD_STEP_MODE");
+  if (!v.empty()) {
+    const char *x = v.c_str();
+    if (env_is(x, "signal") || env_is(x, "signal-only"))
+      c.bad_step_recovery = TMNN_BAD_STEP_SIGNAL_ONLY;
+    else if (env_is(x, "throw") || env_is(x, "strict"))
+      c.bad_step_recovery = TMNN_BAD_STEP_THROW;
+    else if (env_is(x, "skip"))
+      c.bad_step_recovery = TMNN_BAD_STEP_SKIP;
+    else if (env_is(x, "rollback") || env_is(x, "revert"))
+      c.bad_step_recovery = TMNN_BAD_STEP_ROLLBACK;
+    else if (env_is(x, "fallback") || env_is(x, "fallback-and-retry") ||
+             env_is(x, "fallback-and-retry-with-safe-family") ||
+             env_is(x, "safe-family-fallback"))
+      c.bad_step_recovery = TMNN_BAD_STEP_SAFE_FAMILY_RETRY;
+  }
+}
 
 // KernelSpec::validate (kernel_spec.cpp:12-44) plus this build's limits.
 void validate(const tmnn_spec &s) {
@@ -513,8 +615,18 @@ AdamArgs adam_args(const tmnn_ctx &c) {
   return a;
 }
 
-void adam(tmnn_ctx &c) {
-  const AdamArgs a = adam_args(c);
+// Launches the numerics probe over the (reduced) gradients of this rank's
+// parameters, before Adam; see k_numerics_probe.
+void probe_numerics(tmnn_ctx &c, bool force, bool gate) {
+  launch_numerics_probe(adam_args(c), c.params.p, c.m.p, c.v.p, c.gh_fixed.p,
+                        c.gh_float.p, c.gm.p, c.hash_count, c.stats(),
+                        force ? 1 : 0, gate ? 1 : 0, c.num_sms, c.stream);
+  c.launches++;
+}
+
+void adam(tmnn_ctx &c, const StepStats *guard = nullptr) {
+  AdamArgs a = adam_args(c);
+  a.guard = guard;
   launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
               c.touched.p, c.table_h.p, c.num_sms, c.stream);
   c.launches += 2;
@@ -537,7 +649,8 @@ bool can_shard(const tmnn_ctx &c) {
          c.slots % (uint64_t)c.world == 0;
 }
 
-void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm) {
+void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
+               bool probe = false, bool gate = false) {
   const size_t shard = c.hash_count / c.world, off = shard * c.rank;
   const size_t sslots = c.slots / c.world, soff = sslots * c.rank;
   NK(ncclGroupStart());
@@ -557,7 +670,27 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm) {
                      c.comm, c.stream));
   NK(ncclGroupEnd());
   if (after_comm) CK(cudaEventRecord(after_comm, c.stream));
-  const AdamArgs a = adam_args(c);
+  AdamArgs a = adam_args(c);
+  if (probe) {
+    // probe this rank's shard of the table and the (replicated) MLP, then
+    // combine over the ranks so every rank takes the same decision
+    AdamArgs ap = a;
+    ap.hash_count = shard;
+    launch_numerics_probe(ap, c.params.p + off, c.m.p + off, c.v.p + off,
+                          c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
+                          c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                          c.hash_count - off, c.stats(), 1, gate ? 1 : 0,
+                          c.num_sms, c.stream);
+    c.launches++;
+    StepStats *st = c.stats();
+    NK(ncclGroupStart());
+    NK(ncclAllReduce(&st->grad_l2, &st->grad_l2, 1, ncclFloat64, ncclSum,
+                     c.comm, c.stream));
+    NK(ncclAllReduce(&st->max_abs_grad, &st->max_abs_grad, 4, ncclFloat32,
+                     ncclMax, c.comm, c.stream));
+    NK(ncclGroupEnd());
+    a.guard = st;
+  }
   AdamArgs ah = a;
   ah.hash_count = shard;
   ah.slots = sslots;
@@ -634,7 +767,8 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   CK(cudaDeviceGetAttribute(&c.num_sms, cudaDevAttrMultiProcessorCount, device));
   CK(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
   for (auto &e : c.ev) CK(cudaEventCreate(&e));
-  CK(cudaMallocHost(&c.h_loss, sizeof(double)));
+  CK(cudaMallocHost(&c.h_stats, sizeof(StepStats)));
+  c.h_loss = &c.h_stats->loss;
   c.spec = spec;
   c.cfg = cfg;
   c.nd = make_dims(spec, cfg);
@@ -659,7 +793,16 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
     c.gh_float.alloc(c.hash_count);
   c.gm.alloc(c.mlp_count);
   c.touched.alloc(c.slots);
-  c.loss_acc.alloc(1);
+  static_assert(sizeof(StepStats) % sizeof(double) == 0, "StepStats size");
+  c.loss_acc.alloc(sizeof(StepStats) / sizeof(double));
+  c.guard.mode = cfg.numerics_sampling_mode;
+  c.guard.interval = cfg.numerics_sample_interval > 0
+                         ? (uint32_t)cfg.numerics_sample_interval
+                         : 128u;
+  if (cfg.numerics_sampling_mode < 0 || cfg.numerics_sampling_mode > 3)
+    throw std::invalid_argument("numerics_sampling_mode out of range");
+  if (cfg.bad_step_recovery < 0 || cfg.bad_step_recovery > 4)
+    throw std::invalid_argument("bad_step_recovery out of range");
   const size_t sf = exact_scratch_floats(c.nd, c.num_sms);
   if (sf) c.scratch.alloc(sf);
   init_weights(c);
@@ -671,6 +814,85 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   CK(cudaGetLastError());
 }
 
+// activate_safe_family (default_trainer.cpp:1860-1866): from now on this
+// context trains with the fp32 reference-order kernels.
+void activate_safe_family(tmnn_ctx &c) {
+  c.safe_family_active = true;
+  c.family = TMNN_FAMILY_SAFE_DEBUG;
+  c.implicit_touch = false;  // the fp32 kernels store touched bytes
+  c.plan_text += " -> SafeDebug after a numerics anomaly";
+}
+
+// One forward/backward + update of an already staged (and sorted) batch,
+// ending with the read-back of the step statistics.  `force` probes the
+// gradients whatever the loss; `gate` lets an anomaly veto the update.
+void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
+              float inv_N, bool prof, bool force, bool gate) {
+  CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(StepStats), c.stream));
+  if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
+  fwd_bwd(c, p, t, nullptr, N, inv_N);
+  if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
+  if (can_shard(c)) {
+    // sharded: the probe needs a cross-rank combine, so it runs only on
+    // forced steps (sampled steps and every step of a recovery mode)
+    dp_update(c, true, prof ? c.ev[3] : nullptr, force, gate);
+  } else {
+    allreduce_grads(c, true);
+    if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
+    probe_numerics(c, force, gate);
+    adam(c, c.stats());
+  }
+  if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
+  CK(cudaMemcpyAsync(c.h_stats, c.loss_acc.p, sizeof(StepStats),
+                     cudaMemcpyDeviceToHost, c.stream));
+  if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  CK(cudaGetLastError());
+}
+
+// NumericsReport of the last run_step (make_numerics_report,
+// training_step_execution.cpp:409-456): finite_forward from the loss, the
+// rest from the probe when it ran.
+struct StepReport {
+  float mean_loss = 0.0f, grad_norm = 0.0f, max_g = 0.0f, max_u = 0.0f;
+  bool ff = true, fb = true, fu = true, probed = false;
+  bool anomaly() const { return !ff || !fb || !fu; }
+};
+
+StepReport read_report(const tmnn_ctx &c, uint64_t global_n) {
+  const StepStats &h = *c.h_stats;
+  StepReport r;
+  // finalize_async_step: mean_loss = total / float(batch_N)
+  // (parameter_store.cpp:303-322)
+  r.mean_loss = global_n ? (float)h.loss / (float)global_n : 0.0f;
+  r.ff = std::isfinite(r.mean_loss);
+  r.probed = h.probed != 0;
+  if (r.probed) {
+    r.fb = h.nonfinite_bwd == 0.0f;
+    r.max_g = h.max_abs_grad;
+    r.grad_norm = (float)std::sqrt(std::max(0.0, h.grad_l2));
+    r.fu = r.fb && h.nonfinite_upd == 0.0f;
+    r.max_u = r.fb ? h.max_abs_update : 0.0f;
+  }
+  return r;
+}
+
+std::string describe(const StepReport &r) {
+  return std::string("forward=") + (r.ff ? "finite" : "nonfinite") +
+         ", backward=" + (r.fb ? "finite" : "nonfinite") +
+         ", update=" + (r.fu ? "finite" : "nonfinite") +
+         ", max_abs_gradient=" + std::to_string(r.max_g) +
+         ", max_abs_update=" + std::to_string(r.max_u);
+}
+
+// The step driver with the numerics guard (finalize_training_step,
+// training_step_execution.cpp:1080-1235): the probe is forced on sampled
+// steps and on every step of a recovery mode; in a recovery mode an anomaly
+// vetoes the update on the device (the gradients are still cleared), and
+// the host then throws (Throw), reports Skipped / RolledBack, or switches
+// to the SafeDebug family and re-runs the step (FallbackAndRetry).  The
+// step counter advances as in the reference (default_trainer.cpp:1032),
+// except when an error is thrown.
 void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
                 uint32_t flags, tmnn_step_result *res) {
   if (N > 0 && (!pos || !tgt))
@@ -682,35 +904,71 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
   const float *p = stage_in(c, pos, (size_t)N * c.nd.d, c.pos_in, flags);
   const float *t = stage_in(c, tgt, (size_t)N * c.nd.O, c.tgt_in, flags);
   if (c.cfg.morton_sort && N > 1) morton_sort(c, p, t, N, &p, &t);
-  CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(double), c.stream));
   const uint64_t global_n = (uint64_t)N * (uint64_t)c.world;
   const float inv_N = global_n ? 1.0f / (float)global_n : 0.0f;
-  if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
-  fwd_bwd(c, p, t, nullptr, N, inv_N);
-  if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
   const uint32_t done = c.step;
-  if (can_shard(c)) {
-    dp_update(c, true, prof ? c.ev[3] : nullptr);
-  } else {
-    allreduce_grads(c, true);
-    if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
-    adam(c);
+  const int mode = c.cfg.bad_step_recovery;
+  const bool gate = mode != TMNN_BAD_STEP_SIGNAL_ONLY;
+  const bool force = gate || c.guard.should_sample(done, false);
+  run_step(c, p, t, N, inv_N, prof, force, gate);
+  StepReport rep = read_report(c, global_n);
+  bool anomaly = rep.anomaly();
+  bool reported = c.guard.should_sample(done, anomaly);
+  if (reported) c.guard.record(done, anomaly);
+  int action = TMNN_RECOVERY_NONE;
+  if (anomaly && gate) {
+    if (mode == TMNN_BAD_STEP_THROW) {
+      c.step = done;
+      throw OperationFailed("training_step: numerics anomaly detected at step " +
+                            std::to_string(done) + " (" + describe(rep) + ")");
+    } else if (mode == TMNN_BAD_STEP_SKIP) {
+      action = TMNN_RECOVERY_SKIPPED;
+      ++c.n_skipped;
+    } else if (mode == TMNN_BAD_STEP_ROLLBACK) {
+      action = TMNN_RECOVERY_ROLLED_BACK;
+      ++c.n_rolled_back;
+    } else {
+      if (c.safe_family_active || c.family == TMNN_FAMILY_SAFE_DEBUG) {
+        c.step = done;
+        throw OperationFailed(
+            "training_step: numerics anomaly persisted while SafeDebug is "
+            "already active at step " + std::to_string(done) + " (" +
+            describe(rep) + ")");
+      }
+      activate_safe_family(c);
+      c.step = done;  // the vetoed update is re-done with the same step
+      run_step(c, p, t, N, inv_N, prof, true, true);
+      rep = read_report(c, global_n);
+      anomaly = rep.anomaly();
+      c.guard.record(done, anomaly);
+      reported = true;
+      if (anomaly) {
+        c.step = done;
+        throw OperationFailed(
+            "training_step: SafeDebug retry still produced a numerics anomaly "
+            "at step " + std::to_string(done) + " (" + describe(rep) + ")");
+      }
+      action = TMNN_RECOVERY_RETRIED_WITH_SAFE_FAMILY;
+      ++c.n_safe_recoveries;
+    }
   }
-  if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
-  CK(cudaMemcpyAsync(c.h_loss, c.loss_acc.p, sizeof(double),
-                     cudaMemcpyDeviceToHost, c.stream));
-  if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
-  CK(cudaStreamSynchronize(c.stream));
-  CK(cudaGetLastError());
   if (res) {
     std::memset(res, 0, sizeof *res);
-    // finalize_async_step: mean_loss = total / float(batch_N)
-    // (parameter_store.cpp:303-322)
-    res->loss = global_n ? (float)*c.h_loss / (float)global_n : 0.0f;
+    res->loss = rep.mean_loss;
     res->step = done;
     res->batch_size = N;
-    res->numerics_ok = std::isfinite(res->loss) ? 1 : 0;
+    res->numerics_ok = anomaly ? 0 : 1;
     res->family = c.family;
+    res->grad_norm = rep.grad_norm;
+    res->finite_forward = rep.ff;
+    res->finite_backward = rep.fb;
+    res->finite_update = rep.fu;
+    res->max_abs_gradient = rep.max_g;
+    res->max_abs_update = rep.max_u;
+    res->numerics_probed = rep.probed;
+    res->numerics_reported = reported;
+    res->has_numerics_anomaly = anomaly;
+    res->recovery_action = action;
     if (prof) {
       CK(cudaEventElapsedTime(&res->gpu_ms, c.ev[0], c.ev[5]));
       CK(cudaEventElapsedTime(&res->sort_ms, c.ev[0], c.ev[1]));
@@ -823,6 +1081,28 @@ void tmnn_cuda_default_train_cfg(tmnn_train_cfg *c) {
   c->hash_grad_format = TMNN_GRAD_FIXED16;
   c->morton_sort = 1;
   c->sparse_hash_adam = -1;
+  // load_runtime_policy (src/tiny_metal_nn/runtime/runtime_policy.h:144-175)
+  c->numerics_sampling_mode = TMNN_NUMERICS_SAMPLED;
+  c->numerics_sample_interval = 128;
+  c->bad_step_recovery = TMNN_BAD_STEP_SIGNAL_ONLY;
+  apply_policy_env(*c);
+}
+
+tmnn_status tmnn_cuda_get_numerics_stats(tmnn_ctx *c, tmnn_numerics_stats *o) {
+  REQUIRE_CTX(c);
+  if (!o) {
+    g_last_error = "null argument";
+    return TMNN_ERR_NULL_OBJECT;
+  }
+  std::memset(o, 0, sizeof *o);
+  o->reports = c->guard.report_count;
+  o->anomalies = c->guard.anomaly_count;
+  o->skipped = c->n_skipped;
+  o->rolled_back = c->n_rolled_back;
+  o->safe_family_recoveries = c->n_safe_recoveries;
+  o->last_anomaly_step = c->guard.last_anomaly_step;
+  o->safe_family_active = c->safe_family_active ? 1 : 0;
+  return TMNN_OK;
 }
 
 tmnn_status tmnn_cuda_validate_spec(const tmnn_spec *spec) {

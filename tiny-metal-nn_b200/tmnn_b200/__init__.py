@@ -250,6 +250,30 @@ class Trainer:
         self.last_result = res
         return res.loss
 
+    def last_numerics(self):
+        """NumericsReport of the last training step (dict), with the
+        recovery action the guard took."""
+        r = self.last_result
+        if r is None:
+            return None
+        return {"finite_forward": bool(r.finite_forward),
+                "finite_backward": bool(r.finite_backward),
+                "finite_update": bool(r.finite_update),
+                "max_abs_gradient": r.max_abs_gradient,
+                "max_abs_update": r.max_abs_update,
+                "grad_norm": r.grad_norm,
+                "probed": bool(r.numerics_probed),
+                "reported": bool(r.numerics_reported),
+                "anomaly": bool(r.has_numerics_anomaly),
+                "recovery_action": _abi.RECOVERY_ACTION[r.recovery_action]}
+
+    def numerics_stats(self):
+        """Counters of the numerics guard (dict)."""
+        s = _abi.NumericsStats()
+        _check(lib.tmnn_cuda_get_numerics_stats(self._handle(), C.byref(s)),
+               "numerics_stats")
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
     def forward_backward(self, input, target):
         """Accumulate gradients of the internal loss (no optimizer step);
         returns the summed loss of the batch."""

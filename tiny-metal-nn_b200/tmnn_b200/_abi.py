@@ -50,7 +50,10 @@ class TrainCfg(C.Structure):
                 ("hash_grad_format", C.c_int32), ("morton_sort", C.c_int32),
                 ("sparse_hash_adam", C.c_int32), ("active_levels", C.c_int32),
                 ("dp_replicated_optimizer", C.c_int32),
-                ("reserved", C.c_int32 * 6)]
+                ("numerics_sampling_mode", C.c_int32),
+                ("numerics_sample_interval", C.c_int32),
+                ("bad_step_recovery", C.c_int32),
+                ("reserved", C.c_int32 * 3)]
 
 
 class StepResult(C.Structure):
@@ -58,7 +61,29 @@ class StepResult(C.Structure):
                 ("batch_size", C.c_uint32), ("numerics_ok", C.c_int32),
                 ("gpu_ms", C.c_float), ("family", C.c_int32),
                 ("sort_ms", C.c_float), ("fwd_bwd_ms", C.c_float),
-                ("allreduce_ms", C.c_float), ("adam_ms", C.c_float)]
+                ("allreduce_ms", C.c_float), ("adam_ms", C.c_float),
+                ("grad_norm", C.c_float), ("finite_forward", C.c_int32),
+                ("finite_backward", C.c_int32), ("finite_update", C.c_int32),
+                ("max_abs_gradient", C.c_float), ("max_abs_update", C.c_float),
+                ("numerics_probed", C.c_int32),
+                ("numerics_reported", C.c_int32),
+                ("has_numerics_anomaly", C.c_int32),
+                ("recovery_action", C.c_int32)]
+
+
+class NumericsStats(C.Structure):
+    _fields_ = [("reports", C.c_uint64), ("anomalies", C.c_uint64),
+                ("skipped", C.c_uint64), ("rolled_back", C.c_uint64),
+                ("safe_family_recoveries", C.c_uint64),
+                ("last_anomaly_step", C.c_uint32),
+                ("safe_family_active", C.c_int32)]
+
+
+SAMPLING = {"Sampled": 0, "Periodic": 1, "FullPerStep": 2, "Disabled": 3}
+BAD_STEP = {"SignalOnly": 0, "Throw": 1, "Skip": 2, "Rollback": 3,
+            "FallbackAndRetryWithSafeFamily": 4}
+RECOVERY_ACTION = {0: "None", 1: "Skipped", 2: "RolledBack",
+                   3: "RetriedWithSafeFamily"}
 
 
 class BufferView(C.Structure):
@@ -100,6 +125,7 @@ _SIGS = [
     ("tmnn_cuda_adam_step", C.c_int, [P]),
     ("tmnn_cuda_evaluate", C.c_int, [P, P, P, u32, u32]),
     ("tmnn_cuda_evaluate_with_gradient", C.c_int, [P, P, P, P, u32, u32]),
+    ("tmnn_cuda_get_numerics_stats", C.c_int, [P, C.POINTER(NumericsStats)]),
     ("tmnn_cuda_debug_encode", C.c_int, [P, P, u32, P, P, P]),
     ("tmnn_cuda_export_opt_state", C.c_int,
      [P, P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(u32)]),
