@@ -321,6 +321,46 @@ tmnn_status tmnn_cuda_evaluate_with_gradient(tmnn_ctx *ctx,
                                              float *outputs, float *gradients,
                                              uint32_t n, uint32_t flags);
 
+/* NeRF-style field (the benchmark's NeRF configuration; tmnn itself has no
+ * SH encoding and no chained networks, so nothing here replaces a reference
+ * entry point): a density network (the HashGrid + FullyFusedMLP of
+ * `density`, 3D input, 16 outputs, sigma = exp(output 0)) and a colour
+ * network on [SH degree 4 of the unit view direction (16) | density outputs
+ * 1..15 | a zero pad] -> sigmoid RGB.  Loss per sample:
+ * sum_c (rgb_c - rgb_t,c)^2 + (sigma - sigma_t)^2, averaged over the batch.
+ * Adam (lr, beta 0.9/0.99, eps 1e-15) on both networks. */
+typedef struct tmnn_nerf tmnn_nerf;
+typedef struct tmnn_nerf_cfg {
+  tmnn_spec density;           /* spatial_dims 3, num_outputs 16 */
+  float lr;
+  uint32_t color_width;        /* 64 or 128 */
+  uint32_t color_hidden_layers;/* 1..4 */
+  int32_t family;              /* density network family (tmnn_family) */
+  uint64_t seed;
+} tmnn_nerf_cfg;
+tmnn_status tmnn_cuda_nerf_create(int device, const tmnn_nerf_cfg *cfg,
+                                  tmnn_nerf **out);
+tmnn_status tmnn_cuda_nerf_destroy(tmnn_nerf *nerf);
+/* The density network's context (owned by the nerf object): weights,
+ * buffers and plan through the tmnn_cuda_* context calls. */
+tmnn_status tmnn_cuda_nerf_density(tmnn_nerf *nerf, tmnn_ctx **density);
+/* Colour network weights in the reference MLP layout (fp32); writing them
+ * resets its Adam state. */
+tmnn_status tmnn_cuda_nerf_color_weights(tmnn_nerf *nerf, const float *host_in,
+                                         float *host_out, size_t count);
+/* One training step on n samples: positions [n x 3], unit directions
+ * [n x 3], target RGB [n x 3], target density [n]; *loss = mean loss.  Host
+ * pointers, or device pointers with TMNN_PTR_DEVICE. */
+tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *nerf, const float *positions,
+                                      const float *directions,
+                                      const float *rgb, const float *sigma,
+                                      uint32_t n, uint32_t flags, float *loss);
+/* rgb [n x 3] (after the sigmoid) and sigma [n] (after exp). */
+tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *nerf, const float *positions,
+                                     const float *directions, float *rgb,
+                                     float *sigma, uint32_t n, uint32_t flags);
+const char *tmnn_cuda_nerf_last_error(void);
+
 /* Numerics guard counters of this context. */
 tmnn_status tmnn_cuda_get_numerics_stats(tmnn_ctx *ctx,
                                          tmnn_numerics_stats *out);

@@ -70,6 +70,10 @@ def _load():
     lib.tmo_forward.argtypes = [sp, P, P, P, C.c_int64, P]
     lib.tmo_mlp_forward.argtypes = [sp, P, P, C.c_int64, P]
     lib.tmo_eval_gradient.argtypes = [sp, P, P, P, C.c_int64, P, P]
+    lib.tmo_mlp_train.restype = C.c_double
+    lib.tmo_mlp_train.argtypes = [sp, P, P, P, C.c_int64, C.c_int64, C.c_int,
+                                  P, P]
+    lib.tmo_sh4.argtypes = [C.c_float, C.c_float, C.c_float, P]
     lib.tmo_fwd_bwd.restype = C.c_double
     lib.tmo_fwd_bwd.argtypes = [sp, P, P, P, P, P, C.c_int64, C.c_int64, P, P,
                                 P, P, P]
@@ -324,3 +328,109 @@ class OracleTrainer:
 
     def evaluate(self, pos):
         return forward(self.s, self.w[:self.hc], self.w[self.hc:], pos)
+
+
+# ------------------------------------------------------------ NeRF field
+
+def sh4(dirs):
+    """Real SH (16 coefficients) of unit directions [N x 3]."""
+    dirs = np.ascontiguousarray(dirs, np.float32)
+    out = np.zeros((dirs.shape[0], 16), np.float32)
+    for i in range(dirs.shape[0]):
+        lib.tmo_sh4(float(dirs[i, 0]), float(dirs[i, 1]), float(dirs[i, 2]),
+                    out[i].ctypes.data_as(C.c_void_p))
+    return out
+
+
+def mlp_train(s, mlp, x, tgt, inv_count, out_act, grad_mlp):
+    """(loss_sum, dx) of a plain-MLP training pass; grad_mlp accumulates."""
+    x = np.ascontiguousarray(x, np.float32)
+    tgt = np.ascontiguousarray(tgt, np.float32)
+    dx = np.zeros_like(x)
+    loss = lib.tmo_mlp_train(C.byref(s), _p(np.ascontiguousarray(mlp, np.float32)),
+                             _p(x), _p(tgt), x.shape[0], inv_count, out_act,
+                             _p(grad_mlp), _p(dx))
+    return loss, dx
+
+
+def color_spec(W=64, H=2):
+    """The colour network as a plain MLP: 32 inputs (SH 16 | geometry 15 |
+    pad 1), sigmoid RGB, L2."""
+    return make_spec(L=32, F=1, log2T=1, d=3, W=W, H=H, O=3, loss="L2",
+                     grad_mode=GRAD_FLOAT)
+
+
+def _color_input(dirs, dens):
+    x = np.zeros((dirs.shape[0], 32), np.float32)
+    x[:, :16] = sh4(dirs)
+    x[:, 16:31] = dens[:, 1:16]
+    return x
+
+
+class OracleNerf:
+    """CPU restatement of the NeRF-style field step (density HashGrid+MLP ->
+    16 outputs, sigma = exp(out0); colour MLP on [SH(dir) | out 1..15 | 0]
+    -> sigmoid RGB; loss sum_c (rgb-rgb_t)^2 + (sigma-sigma_t)^2 averaged;
+    Adam on both).  Parity unpinned: the reference has no such network."""
+
+    def __init__(self, sd, table, dmlp, cmlp, color_W=64, color_H=2, lr=1e-2):
+        self.sd = sd
+        self.sc = color_spec(color_W, color_H)
+        self.w = np.concatenate([table, dmlp]).astype(np.float32)
+        self.m = np.zeros_like(self.w)
+        self.v = np.zeros_like(self.w)
+        self.hc = table.size
+        self.cw = np.array(cmlp, np.float32)
+        self.cm = np.zeros_like(self.cw)
+        self.cv = np.zeros_like(self.cw)
+        self.lr = lr
+        self.step = 0
+
+    def inference(self, pos, dirs):
+        dens = forward(self.sd, self.w[:self.hc], self.w[self.hc:], pos)
+        z = mlp_forward(self.sc, self.cw, _color_input(dirs, dens))
+        return 1.0 / (1.0 + np.exp(-z)), np.exp(dens[:, 0])
+
+    def training_step(self, pos, dirs, rgb, sigma):
+        N = pos.shape[0]
+        table, dmlp = self.w[:self.hc].copy(), self.w[self.hc:].copy()
+        dens = forward(self.sd, table, dmlp, pos)
+        gc = np.zeros_like(self.cw)
+        lc, dx = mlp_train(self.sc, self.cw, _color_input(dirs, dens), rgb, N,
+                           1, gc)
+        s = np.exp(dens[:, 0].astype(np.float32))
+        r = (s - sigma).astype(np.float32)
+        dy = np.zeros((N, 16), np.float32)
+        dy[:, 0] = (np.float32(2.0) * r) * s * np.float32(1.0 / N)
+        dy[:, 1:16] = dx[:, 16:31]
+        ld = float(np.sum(r.astype(np.float64) ** 2))
+        cfg = AdamCfg(self.lr, self.lr, 0.9, 0.99, 1e-15, 0.0, 0.0, 0.0, 0.0,
+                      self.step, 0, 1)
+        lib.tmo_adam(C.byref(cfg), _p(self.cw), _p(self.cm), _p(self.cv), 0,
+                     self.cw.size, None, None, _p(gc), None, 1)
+        _, g, _ = fwd_bwd(self.sd, table, dmlp, pos, None, d_out=dy)
+        adam(self.sd, self.w, self.m, self.v, g, self.step, lr_hash=self.lr,
+             lr_mlp=self.lr)
+        self.step += 1
+        return (lc + ld) / N
+
+
+def nerf_batch(n, seed):
+    """Seeded NeRF samples: positions U[0,1)^3, unit directions (normalised
+    Gaussians), smooth targets: RGB = sigmoid of 8 random sinusoids of the
+    position per channel plus a linear term in the direction; density =
+    4 sigmoid(sum of 8 sinusoids)."""
+    rng = np.random.default_rng(seed)
+    pos = rng.random((n, 3), dtype=np.float32)
+    d = rng.normal(size=(n, 3)).astype(np.float32)
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    fr = np.random.default_rng(1234)
+    k = fr.normal(size=(4, 8, 3)) * 4.0
+    ph = fr.uniform(0, 2 * np.pi, (4, 8))
+    a = fr.normal(size=(4, 8)) * 0.5
+    dirw = fr.normal(size=(3, 3)) * 0.3
+    f = np.einsum("nd,ckd->nck", pos.astype(np.float64), k) + ph[None]
+    f = (np.sin(f) * a[None]).sum(-1)  # [n, 4]
+    rgb = 1.0 / (1.0 + np.exp(-(f[:, :3] + d.astype(np.float64) @ dirw)))
+    sigma = 4.0 / (1.0 + np.exp(-f[:, 3]))
+    return pos, d, rgb.astype(np.float32), sigma.astype(np.float32)

@@ -1086,3 +1086,105 @@ void tmo_eval_gradient(const tmo_spec *s, const float *table, const float *mlp,
     for (int a = 0; a < d; ++a) grad[i * d + a] = gp[a];
   }
 }
+
+/* ------------------------------------------- plain MLP training, SH */
+
+/* Forward, loss and backward of a plain MLP (no encoding) on inputs x
+ * [N x In] (In = L*F), the arithmetic of forward_point / backward without
+ * the hash parts.  out_act 1 applies a sigmoid to every output; the loss
+ * (point_loss against tgt) is then on the activated outputs and its
+ * gradient passes through y (1 - y).  Accumulates grad_mlp, writes dL/dx to
+ * dx [N x In] when non-NULL, returns the summed loss. */
+double tmo_mlp_train(const tmo_spec *s, const float *mlp, const float *x,
+                     const float *tgt, int64_t N, int64_t inv_count,
+                     int out_act, float *grad_mlp, float *dx) {
+  offsets_t o;
+  mlp_offsets(s, &o);
+  const int In = s->L * s->F, W = s->W, H = s->H, O = s->O;
+  const float inv_N = inv_count > 0 ? 1.0f / (float)inv_count : 0.0f;
+  double loss = 0.0;
+  for (int64_t n = 0; n < N; ++n) {
+    float acts[MAX_H][MAX_W], y[MAX_O], d[MAX_O], g[MAX_W], g2[MAX_W];
+    const float *xi = x + n * In;
+    for (int j = 0; j < W; ++j) {
+      float acc = 0.0f;
+      for (int i = 0; i < In; ++i)
+        acc = acc + xi[i] * mlp[o.w_off[0] + (int64_t)i * W + j];
+      const float t = acc + mlp[o.b_off[0] + j];
+      acts[0][j] = t > 0.0f ? t : 0.0f;
+    }
+    for (int k = 1; k < H; ++k)
+      for (int j = 0; j < W; ++j) {
+        float acc = 0.0f;
+        for (int i = 0; i < W; ++i)
+          acc = acc + acts[k - 1][i] * mlp[o.w_off[k] + (int64_t)i * W + j];
+        const float t = acc + mlp[o.b_off[k] + j];
+        acts[k][j] = t > 0.0f ? t : 0.0f;
+      }
+    for (int m = 0; m < O; ++m) {
+      float acc = mlp[o.b_off[H] + m];
+      for (int j = 0; j < W; ++j)
+        acc = acc + acts[H - 1][j] * mlp[o.w_off[H] + (int64_t)j * O + m];
+      y[m] = out_act == 1 ? 1.0f / (1.0f + expf(-acc)) : acc;
+    }
+    loss += point_loss(s, y, tgt + n * O, inv_N, d);
+    if (out_act == 1)
+      for (int m = 0; m < O; ++m) d[m] = d[m] * (y[m] * (1.0f - y[m]));
+    /* output layer */
+    for (int j = 0; j < W; ++j) {
+      float acc = 0.0f;
+      for (int m = 0; m < O; ++m) {
+        grad_mlp[o.w_off[H] + (int64_t)j * O + m] += d[m] * acts[H - 1][j];
+        acc = acc + d[m] * mlp[o.w_off[H] + (int64_t)j * O + m];
+      }
+      g[j] = acts[H - 1][j] > 0.0f ? acc : 0.0f;
+    }
+    for (int m = 0; m < O; ++m) grad_mlp[o.b_off[H] + m] += d[m];
+    for (int k = H - 1; k >= 1; --k) {
+      for (int i = 0; i < W; ++i) {
+        float acc = 0.0f;
+        for (int j = 0; j < W; ++j) {
+          grad_mlp[o.w_off[k] + (int64_t)i * W + j] += g[j] * acts[k - 1][i];
+          acc = acc + g[j] * mlp[o.w_off[k] + (int64_t)i * W + j];
+        }
+        g2[i] = acts[k - 1][i] > 0.0f ? acc : 0.0f;
+      }
+      for (int j = 0; j < W; ++j) {
+        grad_mlp[o.b_off[k] + j] += g[j];
+        g[j] = g2[j];
+      }
+    }
+    for (int i = 0; i < In; ++i) {
+      float acc = 0.0f;
+      for (int j = 0; j < W; ++j) {
+        grad_mlp[o.w_off[0] + (int64_t)i * W + j] += g[j] * xi[i];
+        acc = acc + g[j] * mlp[o.w_off[0] + (int64_t)i * W + j];
+      }
+      if (dx) dx[n * In + i] = acc;
+    }
+    for (int j = 0; j < W; ++j) grad_mlp[o.b_off[0] + j] += g[j];
+  }
+  return loss;
+}
+
+/* Real spherical harmonics of degree < 4 (16 coefficients) of a unit
+ * direction, graphics sign convention (Sloan 2008, appendix). */
+void tmo_sh4(float x, float y, float z, float *o) {
+  const float xx = x * x, yy = y * y, zz = z * z;
+  o[0] = 0.28209479177387814f;
+  o[1] = -0.48860251190291987f * y;
+  o[2] = 0.48860251190291987f * z;
+  o[3] = -0.48860251190291987f * x;
+  o[4] = 1.0925484305920792f * (x * y);
+  o[5] = -1.0925484305920792f * (y * z);
+  o[6] = 0.94617469575755997f * zz - 0.31539156525251999f;
+  o[7] = -1.0925484305920792f * (x * z);
+  o[8] = 0.54627421529603959f * (xx - yy);
+  o[9] = 0.59004358992664352f * y * (yy - 3.0f * xx);
+  o[10] = 2.8906114426405538f * (x * y) * z;
+  o[11] = 0.45704579946446572f * y * (1.0f - 5.0f * zz);
+  o[12] = 0.3731763325901154f * z * (5.0f * zz - 3.0f);
+  o[13] = 0.45704579946446572f * x * (1.0f - 5.0f * zz);
+  o[14] = 1.4453057213202769f * z * (xx - yy);
+  o[15] = 0.59004358992664352f * x * (3.0f * yy - xx);
+}

@@ -77,6 +77,16 @@ void tmo_forward(const tmo_spec *s, const float *table, const float *mlp,
 void tmo_eval_gradient(const tmo_spec *s, const float *table, const float *mlp,
                        const float *pos, int64_t N, float *out, float *grad);
 
+/* Plain MLP training pass on inputs x [N x L*F]: forward, loss of the spec
+ * against tgt (after a sigmoid on every output when out_act == 1), backward;
+ * accumulates grad_mlp, writes dL/dx [N x L*F] to dx when non-NULL and
+ * returns the summed loss.  dL/dy uses 1/inv_count. */
+double tmo_mlp_train(const tmo_spec *s, const float *mlp, const float *x,
+                     const float *tgt, int64_t N, int64_t inv_count,
+                     int out_act, float *grad_mlp, float *dx);
+/* Real spherical harmonics of degree < 4 (16 values) of a unit direction. */
+void tmo_sh4(float x, float y, float z, float *out);
+
 /* Plain MLP on given features x [N x L*F] (no encoding). */
 void tmo_mlp_forward(const tmo_spec *s, const float *mlp, const float *x,
                      int64_t N, float *out);

@@ -164,6 +164,8 @@ struct FusedParams {
   int mode;          // 0 internal loss, 1 external dL/dy
   int implicit_touch; // float gradients: a slot with a nonzero sum is touched
                       // (no touched-byte stores)
+  int out_act;        // output activation: 0 none, 1 sigmoid
+  float *dxout;       // D == 0 training: dL/dx [N x In] fp32 (may be null)
 };
 
 // ------------------------------------------------------------- device parts
@@ -527,6 +529,10 @@ __global__ void __launch_bounds__(kThreads)
       const float *bo = reinterpret_cast<const float *>(sm + Ly.sb[H]);
 #pragma unroll
       for (int m = 0; m < kOutCols; ++m) y[m] += bo[m];
+      if (P.out_act == 1) {
+#pragma unroll
+        for (int m = 0; m < kOutCols; ++m) y[m] = 1.0f / (1.0f + expf(-y[m]));
+      }
       if (!TRAIN) {
         if (valid)
           for (int m = 0; m < O; ++m) P.out[(size_t)row * O + m] = y[m];
@@ -543,6 +549,12 @@ __global__ void __launch_bounds__(kThreads)
           } else {
             for (int m = 0; m < O; ++m) d[m] = __ldg(P.dext + (size_t)row * O + m);
           }
+        }
+        if (P.out_act == 1) {
+          // d/dz of sigmoid(z) = y (1 - y): the loss (or the caller's
+          // gradient) is w.r.t. the activated output
+#pragma unroll
+          for (int m = 0; m < kOutCols; ++m) d[m] *= y[m] * (1.0f - y[m]);
         }
 #pragma unroll
         for (int m = 0; m < kOutCols; ++m) {
@@ -672,6 +684,21 @@ __global__ void __launch_bounds__(kThreads)
           }
         }
       }
+    } else {
+      // plain MLP: dL/dx to memory (unscaled fp32), for a caller that
+      // back-propagates further (e.g. into the features of another network)
+      if (P.dxout) {
+        for (int ch = half; ch < n_chunks; ch += 2) {
+          float df[8];
+          tmem_ld8(T_s + lane_base + ch * 8, df);
+          if (!valid) continue;
+          float4 *dst = reinterpret_cast<float4 *>(P.dxout + (size_t)row * In + ch * 8);
+          dst[0] = make_float4(df[0] * P.inv_dscale, df[1] * P.inv_dscale,
+                               df[2] * P.inv_dscale, df[3] * P.inv_dscale);
+          dst[1] = make_float4(df[4] * P.inv_dscale, df[5] * P.inv_dscale,
+                               df[6] * P.inv_dscale, df[7] * P.inv_dscale);
+        }
+      }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -783,7 +810,7 @@ KernelFn pick(int d, int F, int W, bool half) {
   TMNN_PICK(3, 1) TMNN_PICK(3, 2) TMNN_PICK(3, 4)
   TMNN_PICK(4, 1) TMNN_PICK(4, 2) TMNN_PICK(4, 4)
 #undef TMNN_PICK
-  if (d == 0 && !TRAIN) return pick_w<0, 2, false, false>(W);
+  if (d == 0) return pick_w<0, 2, false, TRAIN>(W);
   return nullptr;
 }
 
@@ -942,11 +969,12 @@ int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
 
 int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd,
                       const float *mlp, const __half *x, float *out,
-                      uint32_t N, int num_sms, cudaStream_t st) {
+                      uint32_t N, int num_sms, cudaStream_t st, int out_act) {
   FusedParams P{};
   P.xin = x;
   P.out = out;
   P.N = N;
+  P.out_act = out_act;
   P.dscale = P.inv_dscale = 1.0f;
   tmnn_spec spec{};
   spec.table_dtype = TMNN_DTYPE_F32;
@@ -956,8 +984,39 @@ int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd,
   return launch(ws, n0, spec, mlp, nullptr, false, P, num_sms, st);
 }
 
+int fused_mlp_train(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
+                    const __half *x, const float *tgt, const float *dext,
+                    float inv_N, float *gm, double *loss_acc, float *dx,
+                    uint32_t N, int num_sms, cudaStream_t st, int out_act) {
+  FusedParams P{};
+  P.xin = x;
+  P.tgt = tgt;
+  P.dext = dext;
+  P.gm = gm;
+  P.loss_acc = loss_acc;
+  P.dxout = dx;
+  P.inv_N = inv_N;
+  P.out_act = out_act;
+  int e = 0;
+  frexpf(dext ? (float)(N > 0 ? N : 1) : (inv_N > 0.f ? 1.0f / inv_N : 1.0f), &e);
+  P.dscale = ldexpf(1.0f, e - 1);
+  P.inv_dscale = 1.0f / P.dscale;
+  P.N = N;
+  P.mode = dext ? 1 : 0;
+  tmnn_spec spec{};
+  spec.table_dtype = TMNN_DTYPE_F32;
+  NetDims n0 = nd;
+  n0.d = 0;
+  n0.hash_count = 0;
+  return launch(ws, n0, spec, mlp, nullptr, true, P, num_sms, st);
+}
+
 bool fused_mlp_supported(const NetDims &nd, std::string *why) {
   return shape_ok(nd, false, why);
+}
+
+bool fused_mlp_train_supported(const NetDims &nd, std::string *why) {
+  return shape_ok(nd, true, why);
 }
 
 int fused_error(FusedWorkspace &ws, cudaStream_t st) {

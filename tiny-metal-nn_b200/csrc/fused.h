@@ -40,10 +40,21 @@ int fused_forward(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
                   float *out, uint32_t N, int num_sms, cudaStream_t st);
 // Plain FullyFusedMLP inference (no encoding): x fp16 [N x nd.In], mlp the
 // fp32 weights in the reference layout, out fp32 [N x nd.O].
+// out_act 1 applies a sigmoid to every output.
 int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
                       const __half *x, float *out, uint32_t N, int num_sms,
-                      cudaStream_t st);
+                      cudaStream_t st, int out_act = 0);
 bool fused_mlp_supported(const NetDims &nd, std::string *why);
+// Plain FullyFusedMLP training pass: forward, loss (internal, from tgt with
+// the spec's loss) or the caller's dL/d(output) (dext), backward; weight
+// gradients accumulate into gm, the summed loss into *loss_acc, and dL/dx
+// [N x In] fp32 is written to dx when non-null.  With out_act 1 the outputs
+// (and the loss / dext) are those after a sigmoid.
+int fused_mlp_train(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
+                    const __half *x, const float *tgt, const float *dext,
+                    float inv_N, float *gm, double *loss_acc, float *dx,
+                    uint32_t N, int num_sms, cudaStream_t st, int out_act = 0);
+bool fused_mlp_train_supported(const NetDims &nd, std::string *why);
 // Nonzero when a fused kernel reported a timed-out pipeline wait.
 int fused_error(FusedWorkspace &ws, cudaStream_t st);
 

@@ -61,4 +61,9 @@ void launch_gather_rows(const float *src, int width, const uint32_t *perm,
 void launch_scatter_rows(const float *src, int width, const uint32_t *perm,
                          float *dst, uint32_t N, cudaStream_t st);
 
+// ---- plain MLP helpers (mlp.cu) ----
+void mlp_layout(NetDims &nd);
+void mlp_init_xavier(const NetDims &nd, float *w, uint64_t seed,
+                     cudaStream_t st);
+
 }  // namespace tmnn

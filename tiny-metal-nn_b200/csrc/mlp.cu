@@ -28,6 +28,50 @@ struct tmnn_mlp {
   }
 };
 
+namespace tmnn {
+
+// Reference weight layout (mlp_kernel_emitter.cpp:163-191) of a plain MLP
+// with nd.In inputs: offsets and the total count.
+void mlp_layout(NetDims &nd) {
+  int64_t off = 0;
+  nd.w_off[0] = off;
+  off += (int64_t)nd.In * nd.W;
+  nd.b_off[0] = off;
+  off += nd.W;
+  for (int i = 1; i < nd.H; ++i) {
+    nd.w_off[i] = off;
+    off += (int64_t)nd.W * nd.W;
+    nd.b_off[i] = off;
+    off += nd.W;
+  }
+  nd.w_off[nd.H] = off;
+  off += (int64_t)nd.W * nd.O;
+  nd.b_off[nd.H] = off;
+  off += nd.O;
+  nd.mlp_count = (uint32_t)off;
+}
+
+// Xavier-uniform weights and U(-1/sqrt(fan_in), ...) biases from the Philox
+// stream (the XavierUniform mode of default_trainer.cpp:2090-2096).
+void mlp_init_xavier(const NetDims &nd, float *w, uint64_t seed,
+                     cudaStream_t st) {
+  uint32_t cb = 0;
+  for (int layer = 0; layer <= nd.H; ++layer) {
+    const int fin = layer == 0 ? nd.In : nd.W;
+    const int fout = layer == nd.H ? nd.O : nd.W;
+    const uint64_t wc = (uint64_t)fin * fout;
+    const float b = std::sqrt(6.0f / (float)(fin + fout));
+    launch_init_uniform(w + nd.w_off[layer], wc, -b, b, seed, cb, st);
+    cb += (uint32_t)((wc + 3) / 4);
+    const float bb = 1.0f / std::sqrt((float)fin);
+    launch_init_uniform(w + nd.b_off[layer], (uint64_t)fout, -bb, bb, seed, cb,
+                        st);
+    cb += (uint32_t)((fout + 3) / 4);
+  }
+}
+
+}  // namespace tmnn
+
 namespace {
 thread_local std::string g_mlp_err;
 
@@ -73,42 +117,13 @@ tmnn_status tmnn_cuda_mlp_create(int device, uint32_t n_input, uint32_t width,
     std::string why;
     if (!fused_mlp_supported(nd, &why))
       throw std::invalid_argument("mlp_create: " + why);
-    int64_t off = 0;
-    nd.w_off[0] = off;
-    off += (int64_t)nd.In * nd.W;
-    nd.b_off[0] = off;
-    off += nd.W;
-    for (int i = 1; i < nd.H; ++i) {
-      nd.w_off[i] = off;
-      off += (int64_t)nd.W * nd.W;
-      nd.b_off[i] = off;
-      off += nd.W;
-    }
-    nd.w_off[nd.H] = off;
-    off += (int64_t)nd.W * nd.O;
-    nd.b_off[nd.H] = off;
-    off += nd.O;
-    nd.mlp_count = (uint32_t)off;
+    mlp_layout(nd);
     m->device = device;
     CKM(cudaSetDevice(device));
     CKM(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, device));
     CKM(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
     CKM(cudaMalloc(&m->w, (size_t)nd.mlp_count * 4));
-    // Xavier-uniform weights and U(-1/sqrt(fan_in), ...) biases from the
-    // Philox stream (the XavierUniform mode of default_trainer.cpp:2090-2096)
-    uint32_t cb = 0;
-    for (int layer = 0; layer <= nd.H; ++layer) {
-      const int fin = layer == 0 ? nd.In : nd.W;
-      const int fout = layer == nd.H ? nd.O : nd.W;
-      const uint64_t wc = (uint64_t)fin * fout;
-      const float b = std::sqrt(6.0f / (float)(fin + fout));
-      launch_init_uniform(m->w + nd.w_off[layer], wc, -b, b, seed, cb, m->stream);
-      cb += (uint32_t)((wc + 3) / 4);
-      const float bb = 1.0f / std::sqrt((float)fin);
-      launch_init_uniform(m->w + nd.b_off[layer], (uint64_t)fout, -bb, bb, seed,
-                          cb, m->stream);
-      cb += (uint32_t)((fout + 3) / 4);
-    }
+    mlp_init_xavier(nd, m->w, seed, m->stream);
     CKM(cudaStreamSynchronize(m->stream));
   });
   if (st == TMNN_OK)

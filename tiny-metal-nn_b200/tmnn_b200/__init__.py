@@ -27,7 +27,7 @@ from ._abi import lib
 
 __version__ = "0.1.0"
 __all__ = ["Trainer", "ClosedError", "ConcurrentTrainingStepError",
-           "ConfigError", "DTypeError", "TmnnError", "dp_unique_id",
+           "ConfigError", "DTypeError", "TmnnError", "dp_unique_id", "NerfField",
            "__version__"]
 
 
@@ -156,6 +156,118 @@ def _check_mlp(st):
         raise TmnnError(st, lib.tmnn_cuda_mlp_last_error().decode())
 
 
+class NerfField:
+    """NeRF-style field: HashGrid density network (16 outputs, sigma =
+    exp(out0)) + colour network on [SH4(dir) | geometry out 1..15] with
+    sigmoid RGB, trained jointly (include/tmnn_cuda.h, tmnn_cuda_nerf_*)."""
+
+    def __init__(self, n_levels=16, n_features_per_level=2,
+                 log2_hashmap_size=19, base_resolution=16.0,
+                 per_level_scale=1.382, density_width=64,
+                 density_hidden_layers=1, color_width=64,
+                 color_hidden_layers=2, lr=1e-2, seed=42, family="Auto",
+                 table_dtype="F32", device=0):
+        cfg = _abi.NerfCfg()
+        cfg.density = _abi.Spec(n_levels, n_features_per_level,
+                                log2_hashmap_size, 3, base_resolution,
+                                per_level_scale, density_width,
+                                density_hidden_layers, 16, 0, 1.0,
+                                _abi.DTYPE_F16 if table_dtype == "F16"
+                                else _abi.DTYPE_F32)
+        cfg.lr = lr
+        cfg.color_width = color_width
+        cfg.color_hidden_layers = color_hidden_layers
+        cfg.family = _abi.FAMILY[family]
+        cfg.seed = seed
+        h = C.c_void_p()
+        st = lib.tmnn_cuda_nerf_create(device, C.byref(cfg), C.byref(h))
+        if st != _abi.OK:
+            msg = lib.tmnn_cuda_nerf_last_error().decode()
+            if st == _abi.ERR_INVALID_ARGUMENT:
+                raise ValueError(msg)
+            raise TmnnError(st, msg)
+        self._h = h
+        self.color_count = (32 * color_width + color_width +
+                            (color_hidden_layers - 1) *
+                            (color_width * color_width + color_width) +
+                            color_width * 3 + 3)
+        d = C.c_void_p()
+        _check_nerf(lib.tmnn_cuda_nerf_density(h, C.byref(d)))
+        self.density = Trainer(d, 3, 16)
+        self.density._borrowed = True
+
+    def color_weights(self):
+        out = np.empty(self.color_count, np.float32)
+        _check_nerf(lib.tmnn_cuda_nerf_color_weights(
+            self._h, None, out.ctypes.data_as(C.c_void_p), out.size))
+        return out
+
+    def set_color_weights(self, w):
+        w = np.ascontiguousarray(w, np.float32)
+        _check_nerf(lib.tmnn_cuda_nerf_color_weights(
+            self._h, w.ctypes.data_as(C.c_void_p), None, w.size))
+
+    def _args(self, *arrays):
+        ptrs, flags, n = [], 0, None
+        for a, w in arrays:
+            p, rows, f, _k = _arg(a, "input", w) if w > 1 else _arg(
+                a.reshape(-1, 1) if hasattr(a, "reshape") else a, "input", 1)
+            if n is None:
+                n, flags = rows, f
+            elif rows != n or f != flags:
+                raise ValueError("arrays must match in rows and placement")
+            ptrs.append(p)
+        return ptrs, n, flags
+
+    def training_step(self, pos, dirs, rgb, sigma):
+        (pp, dp, cp, sp), n, flags = self._args((pos, 3), (dirs, 3), (rgb, 3),
+                                                (sigma, 1))
+        loss = C.c_float()
+        _check_nerf(lib.tmnn_cuda_nerf_train_step(self._h, pp, dp, cp, sp, n,
+                                                  flags, C.byref(loss)))
+        return loss.value
+
+    def inference(self, pos, dirs):
+        (pp, dp), n, flags = self._args((pos, 3), (dirs, 3))
+        if flags & _abi.PTR_DEVICE:
+            import torch
+            rgb = torch.empty((n, 3), dtype=torch.float32, device=pos.device)
+            sig = torch.empty((n,), dtype=torch.float32, device=pos.device)
+            rp, sp = C.c_void_p(rgb.data_ptr()), C.c_void_p(sig.data_ptr())
+        else:
+            rgb = np.empty((n, 3), np.float32)
+            sig = np.empty((n,), np.float32)
+            rp = rgb.ctypes.data_as(C.c_void_p)
+            sp = sig.ctypes.data_as(C.c_void_p)
+        _check_nerf(lib.tmnn_cuda_nerf_inference(self._h, pp, dp, rp, sp, n,
+                                                 flags))
+        return rgb, sig
+
+    def stream(self):
+        return self.density.stream()
+
+    def close(self):
+        if self._h is not None:
+            self.density.close()
+            lib.tmnn_cuda_nerf_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _check_nerf(st):
+    if st == _abi.OK:
+        return
+    msg = lib.tmnn_cuda_nerf_last_error().decode()
+    if st == _abi.ERR_INVALID_ARGUMENT:
+        raise ValueError(msg)
+    raise TmnnError(st, msg)
+
+
 def dp_unique_id() -> bytes:
     buf = (C.c_uint8 * 128)()
     _check(lib.tmnn_cuda_dp_unique_id(buf), "dp_unique_id")
@@ -199,7 +311,8 @@ class Trainer:
     # ---------------------------------------------------------- lifetime
     def close(self):
         if self._h is not None:
-            _check(lib.tmnn_cuda_ctx_destroy(self._h), "close")
+            if not getattr(self, "_borrowed", False):
+                _check(lib.tmnn_cuda_ctx_destroy(self._h), "close")
             self._h = None
 
     def closed(self):

@@ -71,6 +71,13 @@ class StepResult(C.Structure):
                 ("recovery_action", C.c_int32)]
 
 
+class NerfCfg(C.Structure):
+    _fields_ = [("density", Spec), ("lr", C.c_float),
+                ("color_width", C.c_uint32),
+                ("color_hidden_layers", C.c_uint32), ("family", C.c_int32),
+                ("seed", C.c_uint64)]
+
+
 class NumericsStats(C.Structure):
     _fields_ = [("reports", C.c_uint64), ("anomalies", C.c_uint64),
                 ("skipped", C.c_uint64), ("rolled_back", C.c_uint64),
@@ -146,6 +153,14 @@ _SIGS = [
     ("tmnn_cuda_mlp_forward", C.c_int, [P, P, P, u32]),
     ("tmnn_cuda_mlp_stream", C.c_int, [P, C.POINTER(P)]),
     ("tmnn_cuda_mlp_last_error", C.c_char_p, []),
+    ("tmnn_cuda_nerf_create", C.c_int, [C.c_int, C.POINTER(NerfCfg), C.POINTER(P)]),
+    ("tmnn_cuda_nerf_destroy", C.c_int, [P]),
+    ("tmnn_cuda_nerf_density", C.c_int, [P, C.POINTER(P)]),
+    ("tmnn_cuda_nerf_color_weights", C.c_int, [P, P, P, C.c_size_t]),
+    ("tmnn_cuda_nerf_train_step", C.c_int,
+     [P, P, P, P, P, u32, u32, C.POINTER(C.c_float)]),
+    ("tmnn_cuda_nerf_inference", C.c_int, [P, P, P, P, P, u32, u32]),
+    ("tmnn_cuda_nerf_last_error", C.c_char_p, []),
     ("tmnn_cuda_last_error", C.c_char_p, []),
     ("tmnn_cuda_launch_count", C.c_int, [P, C.POINTER(C.c_uint64)]),
 ]
