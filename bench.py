@@ -50,6 +50,20 @@ WORKLOADS = {
                     O=4, loss="L2", lr=1e-2, batch=1 << 18, table="F16",
                     desc="4D field, batch 2^18/GPU, HashGrid 16x2 fp16 "
                          "T=2^22, MLP 64x2 -> 4, L2, Adam lr 1e-2"),
+    # BASELINE configs[2] (run with --workload nerf)
+    "nerf": dict(L=16, F=2, log2T=19, d=3, base=16.0, scale=1.382, W=64, H=1,
+                 O=16, loss="L2", lr=1e-2, batch=1 << 20, table="F32",
+                 kind="nerf",
+                 desc="NeRF-style field, 2^20 samples/GPU: HashGrid 16x2 "
+                      "T=2^19 scale 1.382 -> MLP 64x1 -> 16 (exp density), "
+                      "SH4(dir) + 15 geometry -> MLP 64x2 -> sigmoid RGB, "
+                      "L2 on RGB and density, Adam lr 1e-2"),
+    # BASELINE configs[3] (run with --workload mlp_sweep)
+    "mlp_sweep": dict(kind="mlp_sweep", batch=1 << 22,
+                      desc="FullyFusedMLP inference sweep: W 16/32/64/128, "
+                           "H 2/4/8, N 2^16..2^22, fp16 N(0,1) inputs "
+                           "(In = W), Xavier-uniform weights, ReLU, 16 "
+                           "outputs"),
 }
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample of the
@@ -227,6 +241,234 @@ def cpu_baseline(w, seconds=12.0):
             "samples_per_s": sps}
 
 
+def nerf_batch_np(n, seed):
+    """Seeded NeRF samples: positions U[0,1)^3, unit directions (normalised
+    Gaussians), smooth targets: RGB = sigmoid of 8 random sinusoids of the
+    position per channel plus a linear term in the direction; density =
+    4 sigmoid(sum of 8 sinusoids)."""
+    rng = np.random.default_rng(seed)
+    pos = rng.random((n, 3), dtype=np.float32)
+    d = rng.normal(size=(n, 3)).astype(np.float32)
+    d /= np.linalg.norm(d, axis=1, keepdims=True)
+    fr = np.random.default_rng(1234)
+    k = fr.normal(size=(4, 8, 3)) * 4.0
+    ph = fr.uniform(0, 2 * np.pi, (4, 8))
+    a = fr.normal(size=(4, 8)) * 0.5
+    dirw = fr.normal(size=(3, 3)) * 0.3
+    f = np.einsum("nd,ckd->nck", pos.astype(np.float64), k) + ph[None]
+    f = (np.sin(f) * a[None]).sum(-1)
+    rgb = 1.0 / (1.0 + np.exp(-(f[:, :3] + d.astype(np.float64) @ dirw)))
+    sigma = 4.0 / (1.0 + np.exp(-f[:, 3]))
+    return pos, d, rgb.astype(np.float32), sigma.astype(np.float32)
+
+
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        return {}
+
+
+def nerf_cpu_baseline(w, seconds=12.0):
+    """OracleNerf (the restated NeRF step in C, OpenMP forward) on 2048-sample
+    steps of the same network."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as o
+    sd = o.make_spec(L=w["L"], F=w["F"], log2T=w["log2T"], d=3, W=w["W"],
+                     H=w["H"], O=16, base=w["base"], scale=w["scale"],
+                     grad_mode=o.GRAD_FLOAT)
+    hw, mw = o.init_weights(sd)
+    cm = np.random.default_rng(1).uniform(
+        -0.2, 0.2, o.mlp_weight_count(o.color_spec())).astype(np.float32)
+    nerf = o.OracleNerf(sd, hw, mw, cm, lr=w["lr"])
+    n = 2048
+    batch = nerf_batch_np(n, 7)
+    nerf.training_step(*batch)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        nerf.training_step(*batch)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el > seconds or steps >= 40:
+            break
+    sps = steps * n / el
+    return {"value": sps / w["batch"], "unit": "steps/s (2^20-sample batches)",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} OracleNerf steps of {n} samples (density "
+                      "forward, colour forward/backward, density backward, "
+                      f"Adam on both) in {el:.1f} s; value = samples/s / 2^20",
+            "samples_per_s": sps}
+
+
+def run_nerf(args, w, rank, world, local, emit):
+    """NeRF-style field: one step = density forward,
+    colour network train, density backward + scatter, Adam on both, over
+    2^20 samples per GPU (data parallel only as independent replicas)."""
+    import torch
+    import tmnn_b200 as t
+    torch.cuda.set_device(local)
+    nf = t.NerfField(n_levels=w["L"], n_features_per_level=w["F"],
+                     log2_hashmap_size=w["log2T"], base_resolution=w["base"],
+                     per_level_scale=w["scale"], lr=w["lr"],
+                     family=args.family, table_dtype=w["table"], device=local)
+    B = w["batch"]
+    pool = [[torch.from_numpy(a).cuda() for a in nerf_batch_np(B, 1000 * rank + i)]
+            for i in range(2)]
+    stream = torch.cuda.ExternalStream(nf.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    for i in range(args.warmup):
+        nf.training_step(*pool[i % 2])
+    barrier(world)
+    torch.cuda.synchronize()
+    _, l0 = nf.profile()
+    phases, losses = [], []
+    ev0.record(stream)
+    for i in range(args.steps):
+        losses.append(nf.training_step(*pool[i % 2], profile=True))
+        phases.append(nf.profile()[0])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    _, l1 = nf.profile()
+    ck = clocks.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    value = world * args.steps / (ms / 1000.0)
+    unit = "steps/s (2^20-sample batches)"
+    # inference: 2^20 device-resident samples per call
+    q = pool[0][:2]
+    for _ in range(3):
+        nf.inference(*q)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(10):
+        nf.inference(*q)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    inf_sps = world * 10 * B / (max_over_ranks(ev0.elapsed_time(ev1), world) / 1e3)
+    # end to end from pinned host memory
+    hp = []
+    for a in pool[0]:
+        h = torch.empty(a.shape, dtype=torch.float32, pin_memory=True)
+        h.copy_(a)
+        hp.append(h.numpy())
+    for _ in range(3):
+        nf.training_step(*hp)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        nf.training_step(*hp)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    if rank != 0:
+        nf.close()
+        return
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    ph = {k: statistics.mean(p[k] for p in phases) for k in phases[0]}
+    # dominant phase: density backward_accumulate (Morton sort + the fused
+    # forward/backward/scatter kernel); algorithmic bytes per sample: gathers
+    # L*8*F*4 B of the fp32 table + float scatters L*8*F*4 B + positions and
+    # dL/dy (12 + 64 B)
+    per_sample = w["L"] * 8 * w["F"] * 8 + 12 + 64
+    achieved = per_sample * B / (ph["density_backward"] / 1e3) / 1e9
+    line = {
+        "metric": "training steps/s (NeRF field, 2^20-sample batches)",
+        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 table / f16 tensor-core MLPs, f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "nerf", "desc": w["desc"], "batch_per_gpu": B,
+                   "global_batch": B * world, "parallelism": f"replicas{world}",
+                   "l2": "no flush: per-step working set (fp32 table, m, v, "
+                         "gradients, 2^20-sample buffers) exceeds the 126 MB L2"},
+        "samples_per_s": value * B, "inference_samples_per_s": inf_sps,
+        "final_loss": losses[-1], "phase_ms": ph,
+        "roofline": {"kernel": "density backward (Morton sort + fused "
+                               "fwd/bwd/scatter)",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": "measured" if peaks.get("hbm_gbs") else "fallback",
+                     "algorithmic_bytes_per_sample": per_sample,
+                     "traffic": None},
+        "gpu_launches": int(l1 - l0),
+        "clocks": ck,
+        "e2e": {"value": world * args.steps / (e_ms / 1000.0), "unit": unit,
+                "h2d_bytes_per_step": int(sum(a.nbytes for a in hp)),
+                "d2h_bytes_per_step": 4},
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = nerf_cpu_baseline(w)
+    nf.close()
+    emit(line)
+
+
+def run_mlp_sweep(args, w, rank, world, local, emit):
+    """FullyFusedMLP inference sweep; value = samples/s
+    at W=64, H=2, N=2^22; every point with its TFLOP/s against the measured
+    bf16 tensor peak."""
+    import torch
+    import tmnn_b200 as t
+    torch.cuda.set_device(local)
+    peaks = load_peaks()
+    peak = peaks.get("bf16_tflops") or 1590.0
+    pts, head = [], None
+    clocks = ClockSampler(local)
+    clocks.start()
+    for W in (16, 32, 64, 128):
+        for H in (2, 4, 8):
+            net = t.FullyFusedMLP(W, W, H, 16, seed=1, device=local)
+            st = torch.cuda.ExternalStream(net.stream())
+            g = torch.Generator(device="cuda").manual_seed(5)
+            for N in (1 << 16, 1 << 20, 1 << 22):
+                x = torch.randn(N, W, device="cuda", generator=g).half()
+                out = torch.empty(N, 16, device="cuda")
+                for _ in range(max(args.warmup, 3)):
+                    net.forward(x, out)
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 20
+                e0.record(st)
+                for _ in range(reps):
+                    net.forward(x, out)
+                e1.record(st)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1) / reps
+                fl = 2 * (W * W + (H - 1) * W * W + W * 16) * N
+                p = {"W": W, "H": H, "N": N, "samples_per_s": N / ms * 1e3,
+                     "tflops": fl / ms / 1e9, "frac_of_bf16_peak": fl / ms / 1e9 / peak,
+                     "ms": ms}
+                pts.append(p)
+                if (W, H, N) == (64, 2, 1 << 22):
+                    head = p
+            net.close()
+    ck = clocks.stop()
+    best = max(pts, key=lambda p: p["tflops"])
+    if rank != 0:
+        return
+    emit({"metric": "inference samples/s (FullyFusedMLP sweep; headline W=64 "
+                    "H=2 N=2^22)",
+          "value": world * head["samples_per_s"], "unit": "samples/s",
+          "n_gpus": world, "steps": 20, "warmup": max(args.warmup, 3),
+          "ms_per_step": head["ms"], "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None,
+          "dtype": "f16 in / f16 tensor-core / f32 accumulate",
+          "data": "synthetic",
+          "config": {"workload": "mlp_sweep", "desc": w["desc"],
+                     "l2": "no flush: at N = 2^22 the fp16 inputs (134 MB to "
+                           "1 GB) exceed the 126 MB L2; smaller N run from L2 "
+                           "(the sweep measures the tensor pipe)"},
+          "roofline": {"bound": "tensor", "achieved": best["tflops"],
+                       "peak": peak, "unit": "TFLOP/s",
+                       "frac": best["tflops"] / peak, "at": {k: best[k] for k in ("W", "H", "N")},
+                       "peak_source": "measured" if peaks.get("bf16_tflops") else "fallback",
+                       "traffic": None},
+          "sweep": pts, "clocks": ck, "gpu_launches": 20 * len(pts)})
+
+
 def run_reference(args, w):
     """Reference arm: the reference's own code compiled here (oracle/_ref:
     its generated scalar train kernel run as C++ through the Metal shim, its
@@ -323,6 +565,17 @@ def main():
         os.write(json_fd, (json.dumps(obj) + "\n").encode())
 
     rank, world, local = dist_setup(args)
+
+    if w.get("kind") in ("nerf", "mlp_sweep"):
+        if args.impl == "reference":
+            if rank == 0:
+                emit({"impl": "reference",
+                      "unavailable": "tmnn has no NeRF field or standalone MLP "
+                                     "inference path to time"})
+            return
+        fn = run_nerf if w["kind"] == "nerf" else run_mlp_sweep
+        fn(args, w, rank, world, local, emit)
+        return
 
     if args.impl == "reference":
         if rank == 0:

@@ -359,6 +359,12 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *nerf, const float *positions,
 tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *nerf, const float *positions,
                                      const float *directions, float *rgb,
                                      float *sigma, uint32_t n, uint32_t flags);
+/* Device milliseconds of the phases of the last step run with TMNN_PROFILE
+ * (phase_ms[4]: density forward + colour input; colour network train + Adam;
+ * density backward_accumulate, Morton sort included; density Adam), and the
+ * number of kernels this object and its density context launched. */
+tmnn_status tmnn_cuda_nerf_profile(tmnn_nerf *nerf, float *phase_ms,
+                                   uint64_t *launches);
 const char *tmnn_cuda_nerf_last_error(void);
 
 /* Numerics guard counters of this context. */

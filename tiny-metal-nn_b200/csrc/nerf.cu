@@ -171,8 +171,14 @@ struct tmnn_nerf {
   FusedWorkspace ws;
   Buf<float> pos_d, dirs_d, rgb_d, sig_d, dens, dx, dy, out_rgb, out_sig;
   Buf<__half> xin;
+  uint64_t launches = 0;   // kernels launched by this object (not the density
+                           // context's own, which it counts itself)
+  cudaEvent_t ev[5] = {};  // phase boundaries of a profiled step
+  float phase_ms[4] = {};  // density fwd, colour, density bwd, density Adam
   ~tmnn_nerf() {
     if (stream) cudaStreamSynchronize(stream);
+    for (auto e : ev)
+      if (e) cudaEventDestroy(e);
     fused_release(ws);
     if (h_loss) cudaFreeHost(h_loss);
     if (density) tmnn_cuda_ctx_destroy(density);
@@ -201,6 +207,7 @@ void colour_adam(tmnn_nerf &n) {
   a.hash_count = 0;
   a.mlp_count = n.cnd.mlp_count;
   launch_adam_mlp(a, n.cw.p, n.cm.p, n.cv.p, n.cg.p, n.num_sms, n.stream);
+  n.launches++;
   fused_weights_changed(n.ws);
   ++n.step;
 }
@@ -213,6 +220,7 @@ void front(tmnn_nerf &n, const float *pos, const float *dirs, uint32_t N) {
         "nerf: density forward");
   k_nerf_input<<<(N + 255) / 256, 256, 0, n.stream>>>(dirs, n.dens.p, n.xin.p,
                                                        N);
+  n.launches++;
 }
 
 }  // namespace
@@ -266,6 +274,7 @@ tmnn_status tmnn_cuda_nerf_create(int device, const tmnn_nerf_cfg *cfg,
     n->cg.ensure(c.mlp_count);
     n->loss.ensure(2);
     CKN(cudaMallocHost(&n->h_loss, 2 * sizeof(double)));
+    for (auto &e : n->ev) CKN(cudaEventCreate(&e));
     mlp_init_xavier(c, n->cw.p, cfg->seed ^ 0x9E3779B97F4A7C15ull, n->stream);
     CKN(cudaMemsetAsync(n->cm.p, 0, c.mlp_count * 4, n->stream));
     CKN(cudaMemsetAsync(n->cv.p, 0, c.mlp_count * 4, n->stream));
@@ -333,21 +342,34 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *n, const float *pos,
     const float *c = stage(*n, rgb, (size_t)N * 3, n->rgb_d, flags);
     const float *s = stage(*n, sigma, N, n->sig_d, flags);
     const float inv_N = 1.0f / (float)N;
+    const bool prof = flags & TMNN_PROFILE;
+    if (prof) CKN(cudaEventRecord(n->ev[0], n->stream));
     front(*n, p, d, N);
+    if (prof) CKN(cudaEventRecord(n->ev[1], n->stream));
     n->dx.ensure((size_t)N * kColorIn);
     n->dy.ensure((size_t)N * 16);
     CKN(cudaMemsetAsync(n->loss.p, 0, 2 * sizeof(double), n->stream));
-    fused_mlp_train(n->ws, n->cnd, n->cw.p, n->xin.p, c, nullptr, inv_N,
-                    n->cg.p, n->loss.p, n->dx.p, N, n->num_sms, n->stream, 1);
+    n->launches += fused_mlp_train(n->ws, n->cnd, n->cw.p, n->xin.p, c, nullptr,
+                                   inv_N, n->cg.p, n->loss.p, n->dx.p, N,
+                                   n->num_sms, n->stream, 1);
     k_nerf_dens_grad<<<(N + 255) / 256, 256, 0, n->stream>>>(
         n->dens.p, s, n->dx.p, inv_N, n->dy.p, n->loss.p + 1, N);
+    n->launches++;
     colour_adam(*n);
     CKN(cudaMemcpyAsync(n->h_loss, n->loss.p, 2 * sizeof(double),
                         cudaMemcpyDeviceToHost, n->stream));
+    if (prof) CKN(cudaEventRecord(n->ev[2], n->stream));
     check(tmnn_cuda_backward_accumulate(n->density, p, n->dy.p, N,
                                         TMNN_PTR_DEVICE),
           "nerf: density backward");
+    if (prof) CKN(cudaEventRecord(n->ev[3], n->stream));
     check(tmnn_cuda_adam_step(n->density), "nerf: density adam");
+    if (prof) {
+      CKN(cudaEventRecord(n->ev[4], n->stream));
+      CKN(cudaEventSynchronize(n->ev[4]));
+      for (int k = 0; k < 4; ++k)
+        CKN(cudaEventElapsedTime(&n->phase_ms[k], n->ev[k], n->ev[k + 1]));
+    }
     CKN(cudaGetLastError());
     if (fused_error(n->ws, n->stream))
       throw std::runtime_error("nerf: colour kernel pipeline wait timed out");
@@ -376,9 +398,10 @@ tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *n, const float *pos,
       o_rgb = n->out_rgb.p;
       o_sig = n->out_sig.p;
     }
-    fused_mlp_forward(n->ws, n->cnd, n->cw.p, n->xin.p, o_rgb, N, n->num_sms,
-                      n->stream, 1);
+    n->launches += fused_mlp_forward(n->ws, n->cnd, n->cw.p, n->xin.p, o_rgb, N,
+                                     n->num_sms, n->stream, 1);
     k_nerf_sigma<<<(N + 255) / 256, 256, 0, n->stream>>>(n->dens.p, o_sig, N);
+    n->launches++;
     if (!dev) {
       CKN(cudaMemcpyAsync(rgb, o_rgb, (size_t)N * 12, cudaMemcpyDeviceToHost,
                           n->stream));
@@ -388,6 +411,19 @@ tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *n, const float *pos,
     CKN(cudaStreamSynchronize(n->stream));
     CKN(cudaGetLastError());
   });
+}
+
+tmnn_status tmnn_cuda_nerf_profile(tmnn_nerf *n, float *phase_ms,
+                                   uint64_t *launches) {
+  if (!n) return TMNN_ERR_NULL_OBJECT;
+  if (phase_ms)
+    for (int k = 0; k < 4; ++k) phase_ms[k] = n->phase_ms[k];
+  if (launches) {
+    uint64_t d = 0;
+    tmnn_cuda_launch_count(n->density, &d);
+    *launches = n->launches + d;
+  }
+  return TMNN_OK;
 }
 
 const char *tmnn_cuda_nerf_last_error(void) { return g_nerf_err.c_str(); }

@@ -219,9 +219,11 @@ class NerfField:
             ptrs.append(p)
         return ptrs, n, flags
 
-    def training_step(self, pos, dirs, rgb, sigma):
+    def training_step(self, pos, dirs, rgb, sigma, profile=False):
         (pp, dp, cp, sp), n, flags = self._args((pos, 3), (dirs, 3), (rgb, 3),
                                                 (sigma, 1))
+        if profile:
+            flags |= _abi.PROFILE
         loss = C.c_float()
         _check_nerf(lib.tmnn_cuda_nerf_train_step(self._h, pp, dp, cp, sp, n,
                                                   flags, C.byref(loss)))
@@ -242,6 +244,14 @@ class NerfField:
         _check_nerf(lib.tmnn_cuda_nerf_inference(self._h, pp, dp, rp, sp, n,
                                                  flags))
         return rgb, sig
+
+    def profile(self):
+        """(phase milliseconds of the last profiled step, kernel launches)."""
+        ms = (C.c_float * 4)()
+        n = C.c_uint64()
+        _check_nerf(lib.tmnn_cuda_nerf_profile(self._h, ms, C.byref(n)))
+        return {"density_forward": ms[0], "color": ms[1],
+                "density_backward": ms[2], "density_adam": ms[3]}, n.value
 
     def stream(self):
         return self.density.stream()

@@ -160,6 +160,7 @@ _SIGS = [
     ("tmnn_cuda_nerf_train_step", C.c_int,
      [P, P, P, P, P, u32, u32, C.POINTER(C.c_float)]),
     ("tmnn_cuda_nerf_inference", C.c_int, [P, P, P, P, P, u32, u32]),
+    ("tmnn_cuda_nerf_profile", C.c_int, [P, P, C.POINTER(C.c_uint64)]),
     ("tmnn_cuda_nerf_last_error", C.c_char_p, []),
     ("tmnn_cuda_last_error", C.c_char_p, []),
     ("tmnn_cuda_launch_count", C.c_int, [P, C.POINTER(C.c_uint64)]),
