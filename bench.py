@@ -415,14 +415,19 @@ def run_mlp_sweep(args, w, rank, world, local, emit):
     peaks = load_peaks()
     peak = peaks.get("bf16_tflops") or 1590.0
     pts, head = [], None
+    grid = [(W, H, N) for W in (16, 32, 64, 128) for H in (2, 4, 8)
+            for N in (1 << 16, 1 << 20, 1 << 22)]
+    if args.only:
+        W_, H_, n_ = (int(v) for v in args.only.split(":"))
+        grid = [(W_, H_, 1 << n_)]
     clocks = ClockSampler(local)
     clocks.start()
-    for W in (16, 32, 64, 128):
-        for H in (2, 4, 8):
+    for W, H in dict.fromkeys((W, H) for W, H, _ in grid):
+        if True:
             net = t.FullyFusedMLP(W, W, H, 16, seed=1, device=local)
             st = torch.cuda.ExternalStream(net.stream())
             g = torch.Generator(device="cuda").manual_seed(5)
-            for N in (1 << 16, 1 << 20, 1 << 22):
+            for N in [n for w_, h_, n in grid if (w_, h_) == (W, H)]:
                 x = torch.randn(N, W, device="cuda", generator=g).half()
                 out = torch.empty(N, 16, device="cuda")
                 for _ in range(max(args.warmup, 3)):
@@ -447,6 +452,7 @@ def run_mlp_sweep(args, w, rank, world, local, emit):
             net.close()
     ck = clocks.stop()
     best = max(pts, key=lambda p: p["tflops"])
+    head = head or best
     if rank != 0:
         return
     emit({"metric": "inference samples/s (FullyFusedMLP sweep; headline W=64 "
@@ -552,6 +558,8 @@ def main():
     ap.add_argument("--no-morton", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only", default=None,
+                    help="mlp_sweep: one point W:H:log2N (e.g. 64:4:20)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = WORKLOADS[args.workload]

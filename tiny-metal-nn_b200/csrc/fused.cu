@@ -789,6 +789,332 @@ __global__ void k_pack(NetDims nd, Layout Ly, const float *__restrict__ mlp,
     reinterpret_cast<float *>(img + Ly.b[H])[i] = i < O ? mlp[nd.b_off[H] + i] : 0.f;
 }
 
+// ------------------------------------------------ pipelined MLP inference
+//
+// Plain FullyFusedMLP inference with NG 128-row tiles in flight per CTA.
+// The activations never touch shared memory: each tile keeps, in its own
+// TMEM columns, an fp32 accumulator (W columns) and the fp16 activations
+// that feed the next layer as the MMA's A operand (two per 32-bit column,
+// max(In, W) / 2 columns); only the weights (the B operand) are read from
+// shared memory, so a layer moves W*W*2 bytes of shared memory for
+// 2*128*W*W flops.
+//   warp 0 (one thread)   issues every layer's tcgen05.mma for the NG tiles
+//                         in turn and commits to that tile's mma_done barrier;
+//   warps 4 .. 4+4NG-1    NG epilogue groups of 128 threads, one row each
+//                         (TMEM lane quarter = warp % 4): write the input row
+//                         into the A columns (tcgen05.st), then per layer wait
+//                         mma_done, read the accumulator, add the bias, ReLU,
+//                         store fp16 into the A columns and arrive on
+//                         act_ready; the output layer goes to memory.
+// All weights stay in shared memory (one copy per CTA, one CTA per SM).
+// Every barrier wait is bounded; on a timeout the kernel sets the error word
+// and stops issuing work.
+struct PipeParams {
+  NetDims nd;
+  Layout lay;           // weight image offsets (inference layout)
+  const uint8_t *wimage;
+  const __half *xin;
+  float *out;
+  int *err;
+  uint32_t N, ntiles;
+  uint32_t bar_off;
+  uint32_t gcols;       // TMEM columns per tile (accumulator + A operand)
+  uint32_t tcols;       // allocated TMEM columns
+  int out_act;
+};
+
+__device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(mbar)
+               : "memory");
+}
+
+// D = A . B with A [128 x K] fp16 in TMEM (K/2 columns from a_tmem) and B a
+// core-blocked MN-major shared-memory operand; one thread issues.
+__device__ __forceinline__ void gemm_ta(uint32_t tmem_d, uint32_t a_tmem,
+                                        uint32_t b_base, int b_cols, int N,
+                                        int K) {
+  const uint32_t id = tc::idesc(kTile, N, 0, 1);
+  const uint32_t b_l = (uint32_t)b_cols * 16u, b_s = 128u;
+  for (int s = 0; s < K / 16; ++s) {
+    const uint64_t bd = tc::sdesc(b_base + s * 2u * b_l, b_l, b_s);
+    const uint32_t acc = s > 0 ? 1u : 0u;
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+            tmem_d),
+        "r"(a_tmem + 8u * s), "l"(bd), "r"(id), "r"(acc));
+  }
+}
+
+// 16 / 8 packed fp16 pairs into consecutive TMEM columns of this lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,"
+      "%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+      "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]),
+      "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::
+          "r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]),
+      "r"(v[6]), "r"(v[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <int W, int NG>
+__global__ void __launch_bounds__(128 + 128 * NG)
+    k_mlp_pipe(const __grid_constant__ PipeParams P) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const NetDims &nd = P.nd;
+  const Layout &Ly = P.lay;
+  const int t = threadIdx.x, warp = t >> 5;
+  const int In = nd.In, H = nd.H, O = nd.O;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + P.bar_off);
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(sm + P.bar_off + 16 * NG);
+  {
+    const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage);
+    uint4 *dst = reinterpret_cast<uint4 *>(sm);
+    for (uint32_t i = t; i < Ly.image_bytes / 16; i += blockDim.x) dst[i] = src[i];
+    if (t < NG) {
+      tc::mbar_init(tc::smem_u32(bars + t), 1);         // mma_done[g]
+      tc::mbar_init(tc::smem_u32(bars + NG + t), 128);  // act_ready[g]
+    }
+    if (warp == 0) tc::tmem_alloc(tc::smem_u32(tslot), P.tcols);
+  }
+  tc::fence_proxy_async();
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const uint32_t stride = gridDim.x * NG;
+  bool ok = true;
+
+  if (warp == 0) {
+    if ((t & 31) == 0) {
+      // MMA issuer: round robin over the groups, one layer at a time
+      uint32_t tile[NG], ph[NG];
+      int layer[NG];
+      bool live[NG];
+      int n_live = 0;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        tile[g] = blockIdx.x * NG + g;
+        ph[g] = 0;
+        layer[g] = 0;
+        live[g] = tile[g] < P.ntiles;
+        n_live += live[g];
+      }
+      while (n_live > 0 && ok) {
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          if (!live[g] || !ok) continue;
+          if (!tc::mbar_wait(tc::smem_u32(bars + NG + g), ph[g], kWaitBound)) {
+            ok = false;
+            atomicExch(P.err, 1);
+            break;
+          }
+          ph[g] ^= 1u;
+          tc::fence_after_sync();
+          const int k = layer[g];
+          const uint32_t acc = tmem + (uint32_t)g * P.gcols;
+          const uint32_t a = acc + (uint32_t)W;
+          if (k < H)
+            gemm_ta(acc, a, sbase + Ly.w[k], W, W, k == 0 ? In : W);
+          else
+            gemm_ta(acc, a, sbase + Ly.w[H], kOutCols, kOutCols, W);
+          tc::commit(tc::smem_u32(bars + g));
+          if (k == H) {
+            layer[g] = 0;
+            tile[g] += stride;
+            if (tile[g] >= P.ntiles) {
+              live[g] = false;
+              --n_live;
+            }
+          } else {
+            layer[g] = k + 1;
+          }
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    const int g = (warp - 4) >> 2;
+    const int r = t - 128 - 128 * g;  // row of the tile = TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t acc = tmem + (uint32_t)g * P.gcols + lane_base;
+    const uint32_t a_cols = acc + (uint32_t)W;
+    const uint32_t done_bar = tc::smem_u32(bars + g);
+    const uint32_t ready_bar = tc::smem_u32(bars + NG + g);
+    uint32_t ph = 0;
+    for (uint32_t tile = blockIdx.x * NG + g; tile < P.ntiles && ok;
+         tile += stride) {
+      const uint32_t row = tile * kTile + r;
+      const bool valid = row < P.N;
+      // input row -> A columns (8 fp16 = 4 columns per 16-byte load)
+      for (int c0 = 0; c0 < In; c0 += 16) {
+        uint32_t u[8];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint4 x = make_uint4(0u, 0u, 0u, 0u);
+          if (valid)
+            x = __ldg(reinterpret_cast<const uint4 *>(P.xin + (size_t)row * In + c0) + q);
+          u[4 * q] = x.x;
+          u[4 * q + 1] = x.y;
+          u[4 * q + 2] = x.z;
+          u[4 * q + 3] = x.w;
+        }
+        tmem_st8(a_cols + (uint32_t)(c0 / 2), u);
+      }
+      tmem_st_wait();
+      tc::fence_before_sync();
+      mbar_arrive(ready_bar);
+      for (int k = 0; k <= H && ok; ++k) {
+        if (!tc::mbar_wait(done_bar, ph, kWaitBound)) {
+          ok = false;
+          atomicExch(P.err, 1);
+          break;
+        }
+        ph ^= 1u;
+        tc::fence_after_sync();
+        if (k < H) {
+          const float4 *bk = reinterpret_cast<const float4 *>(sm + Ly.b[k]);
+          constexpr int CH = W < 64 ? W : 64;  // columns per TMEM load wait
+#pragma unroll
+          for (int c0 = 0; c0 < W; c0 += CH) {
+            float v[CH];
+            if (CH == 64)
+              tc::tmem_ld64(acc + c0, v);
+            else if (CH == 32)
+              tc::tmem_ld32(acc + c0, v);
+            else
+              tc::tmem_ld16(acc + c0, v);
+            uint32_t hpk[CH / 2];
+#pragma unroll
+            for (int i = 0; i < CH; i += 4) {
+              const float4 b = bk[(c0 + i) / 4];
+              hpk[i / 2] = pack_h2(fmaxf(v[i] + b.x, 0.f), fmaxf(v[i + 1] + b.y, 0.f));
+              hpk[i / 2 + 1] =
+                  pack_h2(fmaxf(v[i + 2] + b.z, 0.f), fmaxf(v[i + 3] + b.w, 0.f));
+            }
+#pragma unroll
+            for (int q = 0; q < CH / 2; q += 8)
+              tmem_st8(a_cols + (uint32_t)(c0 / 2 + q), hpk + q);
+          }
+          tmem_st_wait();
+          tc::fence_before_sync();
+          mbar_arrive(ready_bar);
+        } else {
+          float y[kOutCols];
+          tc::tmem_ld16(acc, y);
+          tc::fence_before_sync();
+          const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
+#pragma unroll
+          for (int m = 0; m < kOutCols; ++m) {
+            y[m] += bo[m];
+            if (P.out_act == 1) y[m] = 1.0f / (1.0f + expf(-y[m]));
+          }
+          if (valid) {
+            float *o = P.out + (size_t)row * O;
+            if (O == 16) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                reinterpret_cast<float4 *>(o)[q] =
+                    make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+            } else {
+              for (int m = 0; m < O; ++m) o[m] = y[m];
+            }
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, P.tcols);
+  }
+}
+
+constexpr uint32_t kPipeSmemMax = 220 * 1024;
+
+int ensure_packed(FusedWorkspace &ws, const NetDims &nd, const float *params,
+                  cudaStream_t st);
+
+// TMEM columns per tile: W fp32 accumulator columns + max(In, W)/2 columns
+// of fp16 pairs, rounded up to 32.
+uint32_t pipe_gcols(const NetDims &nd) {
+  const uint32_t c = (uint32_t)nd.W + (uint32_t)(nd.In > nd.W ? nd.In : nd.W) / 2;
+  return (c + 31u) & ~31u;
+}
+
+// Tiles in flight: as many as TMEM holds, 2..4; 0 when the weights do not
+// fit in shared memory.
+int pipe_groups(const NetDims &nd) {
+  const Layout L = make_layout(nd, false);
+  if (align128(L.image_bytes) + 128 > kPipeSmemMax) return 0;
+  int ng = (int)(512 / pipe_gcols(nd));
+  if (ng > 4) ng = 4;
+  return ng >= 2 ? ng : 0;
+}
+
+uint32_t pipe_smem(const NetDims &nd) {
+  if (!pipe_groups(nd)) return 0;
+  return align128(make_layout(nd, false).image_bytes) + 128;
+}
+
+int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
+                    const __half *x, float *out, uint32_t N, int num_sms,
+                    cudaStream_t st, int out_act) {
+  int launches = ensure_packed(ws, nd, mlp, st);
+  PipeParams P{};
+  P.nd = nd;
+  P.lay = make_layout(nd, false);
+  P.wimage = (const uint8_t *)ws.wpack + make_layout(nd, true).image_bytes;
+  P.xin = x;
+  P.out = out;
+  P.err = ws.err;
+  P.N = N;
+  P.ntiles = (N + kTile - 1) / kTile;
+  const int NG = pipe_groups(nd);
+  P.bar_off = align128(P.lay.image_bytes);
+  P.gcols = pipe_gcols(nd);
+  P.tcols = 32;
+  while (P.tcols < (uint32_t)NG * P.gcols) P.tcols <<= 1;
+  P.out_act = out_act;
+  const uint32_t smem = pipe_smem(nd);
+  using PipeFn = void (*)(PipeParams);
+  PipeFn fn = nullptr;
+#define TMNN_PIPE(WW)                                      \
+  case WW:                                                 \
+    fn = NG == 2 ? k_mlp_pipe<WW, 2>                       \
+         : NG == 3 ? k_mlp_pipe<WW, 3> : k_mlp_pipe<WW, 4>; \
+    break;
+  switch (nd.W) { TMNN_PIPE(16) TMNN_PIPE(32) TMNN_PIPE(64) TMNN_PIPE(128) }
+#undef TMNN_PIPE
+  if (!fn || !smem) throw std::runtime_error("mlp pipe: unsupported shape");
+  cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)smem);
+  uint32_t grid = (P.ntiles + NG - 1) / NG;
+  if (grid > (uint32_t)num_sms) grid = (uint32_t)num_sms;
+  if (grid == 0) return launches;
+  fn<<<grid, 128 + 128 * NG, smem, st>>>(P);
+  return launches + 1;
+}
+
 using KernelFn = void (*)(FusedParams);
 
 template <int D, int F, bool HALF, bool TRAIN>
@@ -846,17 +1172,17 @@ NetDims dims_of(const tmnn_spec &s) {
   return nd;
 }
 
-int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
-           const float *params, const __half *table_h, bool train,
-           FusedParams &P, int num_sms, cudaStream_t st) {
-  const Layout Ly = make_layout(nd, train);
+// (Re)packs the training and inference weight images when the weights
+// changed; returns the kernels launched.
+int ensure_packed(FusedWorkspace &ws, const NetDims &nd, const float *params,
+                  cudaStream_t st) {
   int launches = 0;
   if (!ws.err) {
     if (cudaMalloc(&ws.err, sizeof(int)) != cudaSuccess)
       throw std::runtime_error("fused: cudaMalloc failed");
     cudaMemsetAsync(ws.err, 0, sizeof(int), st);
   }
-  // (re)pack the weight images when the weights changed
+  const Layout Ly = make_layout(nd, false);
   if (ws.dirty || ws.wpack_bytes < 2ull * Ly.image_bytes) {
     const Layout Lt = make_layout(nd, true), Lf = make_layout(nd, false);
     const size_t need = (size_t)Lt.image_bytes + Lf.image_bytes;
@@ -876,6 +1202,14 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
     launches += 2;
     ws.dirty = false;
   }
+  return launches;
+}
+
+int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
+           const float *params, const __half *table_h, bool train,
+           FusedParams &P, int num_sms, cudaStream_t st) {
+  const Layout Ly = make_layout(nd, train);
+  int launches = ensure_packed(ws, nd, params, st);
   P.nd = nd;
   P.lay = Ly;
   P.wimage = (const uint8_t *)ws.wpack +
@@ -981,6 +1315,8 @@ int fused_mlp_forward(FusedWorkspace &ws, const NetDims &nd,
   NetDims n0 = nd;
   n0.d = 0;
   n0.hash_count = 0;
+  if (!ws.no_pipe && pipe_smem(n0))
+    return launch_mlp_pipe(ws, n0, mlp, x, out, N, num_sms, st, out_act);
   return launch(ws, n0, spec, mlp, nullptr, false, P, num_sms, st);
 }
 

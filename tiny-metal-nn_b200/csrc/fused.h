@@ -22,6 +22,7 @@ struct FusedWorkspace {
   bool dirty = true;
   int ctas_per_sm = 0;
   int *err = nullptr;
+  bool no_pipe = false;  // plain-MLP inference: force the one-tile kernel
 };
 
 bool fused_supported(const tmnn_spec &spec, const tmnn_train_cfg &cfg,
