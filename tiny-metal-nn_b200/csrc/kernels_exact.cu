@@ -1009,6 +1009,182 @@ __global__ void __launch_bounds__(kExactBlock)
   }
 }
 
+// Register-resident variant of k_eval_gradient for the common shapes
+// (W <= 64, H <= 2 supported by the template): the weights sit in shared memory (broadcast reads), the
+// activations and back-propagated gradients in registers (the layer loops
+// are unrolled at compile time), ReLU masks as bits.  Same operations in the
+// same order as k_eval_gradient, so the results are identical.
+template <int W, int H, int F, int D>
+__global__ void __launch_bounds__(kExactBlock)
+    k_eval_gradient_reg(NetDims nd, const float *__restrict__ table,
+                        const float *__restrict__ mlp,
+                        const float *__restrict__ pos, float *__restrict__ out,
+                        float *__restrict__ grad, uint32_t N) {
+  extern __shared__ float sw[];
+  for (uint32_t i = threadIdx.x; i < nd.mlp_count; i += blockDim.x) sw[i] = mlp[i];
+  __syncthreads();
+  constexpr int MW = (W + 31) / 32;
+  const float *W0 = sw + nd.w_off[0];
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < N;
+       i += gridDim.x * blockDim.x) {
+    float p[4];
+#pragma unroll
+    for (int a = 0; a < D; ++a) p[a] = pos[(size_t)i * D + a];
+    float ha[W], hb[W];
+    uint32_t m0[MW];
+#pragma unroll
+    for (int j = 0; j < W; ++j) ha[j] = 0.0f;
+    for (int l = 0; l < nd.L; ++l) {
+      float feat[F];
+      if (D == 4) {
+        Corners c;
+        level_corners(nd, p, l, c);
+        level_features(nd, table, c, feat);
+      } else {
+        int32_t bc[4];
+        float fr[4];
+        level_cell(nd, p, l, bc, fr);
+        float cv[F][2][2][2];
+#pragma unroll
+        for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+          for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+            for (int dx = 0; dx < 2; ++dx) {
+              const float *e = table + corner_offset(nd, l, bc, dx, dy, dz, 0);
+#pragma unroll
+              for (int f = 0; f < F; ++f) cv[f][dz][dy][dx] = e[f];
+            }
+#pragma unroll
+        for (int f = 0; f < F; ++f) feat[f] = trilinear_value_grad(cv[f], fr, nullptr);
+      }
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const float *wr = W0 + (l * F + f) * W;
+#pragma unroll
+        for (int j = 0; j < W; ++j) ha[j] = ha[j] + feat[f] * wr[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const float t = ha[j] + sw[nd.b_off[0] + j];
+      ha[j] = t > 0.0f ? t : 0.0f;
+    }
+    // ha = h0; for H == 2 hb = h1 and ha keeps only its mask
+    if (H == 2) {
+#pragma unroll
+      for (int w = 0; w < MW; ++w) m0[w] = 0u;
+      const float *W1 = sw + nd.w_off[1];
+#pragma unroll
+      for (int j = 0; j < W; ++j) hb[j] = 0.0f;
+#pragma unroll
+      for (int q = 0; q < W; ++q) {
+        const float hq = ha[q];
+        if (hq > 0.0f) m0[q >> 5] |= 1u << (q & 31);
+#pragma unroll
+        for (int j = 0; j < W; ++j) hb[j] = hb[j] + hq * W1[q * W + j];
+      }
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const float t = hb[j] + sw[nd.b_off[1] + j];
+        hb[j] = t > 0.0f ? t : 0.0f;
+      }
+    }
+    const float *wo = sw + nd.w_off[H];
+    float y = sw[nd.b_off[H]];
+    float cur[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const float hv = H == 2 ? hb[j] : ha[j];
+      y = y + hv * wo[j];
+      cur[j] = wo[j] * (hv > 0.0f ? 1.0f : 0.0f);
+    }
+    if (H == 2) {
+      const float *W1 = sw + nd.w_off[1];
+#pragma unroll
+      for (int q = 0; q < W; ++q) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < W; ++j) acc = acc + cur[j] * W1[q * W + j];
+        hb[q] = acc * (((m0[q >> 5] >> (q & 31)) & 1u) ? 1.0f : 0.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < W; ++j) cur[j] = hb[j];
+    }
+    float gp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int l = 0; l < nd.L; ++l) {
+      int32_t bc[4];
+      float fr[4];
+      level_cell(nd, p, l, bc, fr);
+      float dfeat[F];
+#pragma unroll
+      for (int f = 0; f < F; ++f) {
+        const float *wr = W0 + (l * F + f) * W;
+        float gf = 0.0f;
+#pragma unroll
+        for (int j = 0; j < W; ++j) gf = gf + cur[j] * wr[j];
+        dfeat[f] = gf * nd.res[l];
+      }
+      if (D == 4) {
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          float cv[2][2][2][2];
+#pragma unroll
+          for (int dw = 0; dw < 2; ++dw)
+#pragma unroll
+            for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+              for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+                for (int dx = 0; dx < 2; ++dx)
+                  cv[dw][dz][dy][dx] =
+                      table[corner_offset(nd, l, bc, dx, dy, dz, dw) + f];
+          float tg[4];
+          quadrilinear_grad(cv, fr, tg);
+#pragma unroll
+          for (int a = 0; a < 4; ++a) gp[a] = gp[a] + dfeat[f] * tg[a];
+        }
+      } else {
+        float cv[F][2][2][2];
+#pragma unroll
+        for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+          for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+            for (int dx = 0; dx < 2; ++dx) {
+              const float *e = table + corner_offset(nd, l, bc, dx, dy, dz, 0);
+#pragma unroll
+              for (int f = 0; f < F; ++f) cv[f][dz][dy][dx] = e[f];
+            }
+#pragma unroll
+        for (int f = 0; f < F; ++f) {
+          float tg[3];
+          trilinear_value_grad(cv[f], fr, tg);
+#pragma unroll
+          for (int a = 0; a < 3; ++a) gp[a] = gp[a] + dfeat[f] * tg[a];
+        }
+      }
+    }
+    out[i] = y;
+#pragma unroll
+    for (int a = 0; a < D; ++a) grad[(size_t)i * D + a] = gp[a];
+  }
+}
+
+using EvalGradFn = void (*)(NetDims, const float *, const float *,
+                            const float *, float *, float *, uint32_t);
+
+// Instantiated for the shapes of the benchmark configurations (two
+// features per level, 64 wide, one hidden layer -- the single-output SDF
+// shape -- 3D or 4D; with two hidden layers the unrolled code spills); other
+// shapes run k_eval_gradient.
+EvalGradFn pick_eval_grad(const NetDims &nd) {
+  if (nd.F != 2 || nd.W != 64) return nullptr;
+  if (nd.H == 1) return nd.d == 3 ? k_eval_gradient_reg<64, 1, 2, 3>
+                                  : k_eval_gradient_reg<64, 1, 2, 4>;
+  return nullptr;
+}
+
 // ------------------------------------------------------------ launchers
 
 static int wmax_for(int W) {
@@ -1083,6 +1259,14 @@ void launch_eval_gradient(const NetDims &nd, const float *table,
                           cudaStream_t st) {
   if (N == 0) return;
   const int grid = exact_grid(N, num_sms);
+  const size_t wbytes = (size_t)nd.mlp_count * sizeof(float);
+  if (EvalGradFn fn = pick_eval_grad(nd); fn && wbytes <= 96 * 1024) {
+    if (wbytes > 48 * 1024)
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)wbytes);
+    fn<<<grid, kExactBlock, wbytes, st>>>(nd, table, mlp, pos, out, grad, N);
+    return;
+  }
 #define TMNN_EG_CASE(WM)                                                     \
   k_eval_gradient<WM><<<grid, kExactBlock, 0, st>>>(nd, table, mlp, pos, out, \
                                                     grad, N, scratch);
