@@ -77,7 +77,7 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
-def make_config(w, family, grad, morton):
+def make_config(w, family, grad, morton, morton_bits=12):
     return {
         "encoding": {"otype": "HashGrid", "n_levels": w["L"],
                      "n_features_per_level": w["F"],
@@ -89,7 +89,8 @@ def make_config(w, family, grad, morton):
         "loss": {"otype": w["loss"]},
         "optimizer": {"otype": "Adam", "learning_rate": w["lr"]},
         "b200": {"family": family, "hash_grad_format": grad,
-                 "table_dtype": w["table"], "morton_sort": morton},
+                 "table_dtype": w["table"], "morton_sort": morton,
+                 "morton_key_bits": morton_bits},
     }
 
 
@@ -556,6 +557,8 @@ def main():
     ap.add_argument("--family", default="Auto")
     ap.add_argument("--grad", default="F32")
     ap.add_argument("--no-morton", action="store_true")
+    ap.add_argument("--morton-bits", type=int, default=12,
+                    help="Morton sort key bits (0: the whole code)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only", default=None,
@@ -594,7 +597,8 @@ def main():
     import tmnn_b200 as t
     torch.cuda.set_device(local)
     tr = t.Trainer.from_config(make_config(w, args.family, args.grad,
-                                           not args.no_morton),
+                                           not args.no_morton,
+                                           args.morton_bits),
                                n_input=w["d"], n_output=w["O"], device=local)
     if world > 1:
         import torch.distributed as dist
@@ -730,6 +734,7 @@ def main():
                    "parallelism": f"dp{world}", "family": plan["family"],
                    "hash_grad_format": args.grad,
                    "morton_sort": not args.no_morton,
+                   "morton_key_bits": args.morton_bits,
                    "l2": "no flush: per-step working set (fp32 params, m, v, "
                          "grads, fp16 gather copy) exceeds the 126 MB L2"},
         "samples_per_s": value * B,

@@ -126,7 +126,11 @@ typedef struct tmnn_train_cfg {
   int32_t numerics_sampling_mode; /* tmnn_numerics_sampling */
   int32_t numerics_sample_interval; /* steps between sampled probes (128) */
   int32_t bad_step_recovery;      /* tmnn_bad_step_recovery */
-  int32_t reserved[3];
+  int32_t morton_key_bits;        /* Morton sort key: the top k bits of the
+                                     code (1..32); 0 = the whole code (30 bits
+                                     in 3D, 32 in 4D, the reference's order up
+                                     to ties).  Default 12. */
+  int32_t reserved[2];
 } tmnn_train_cfg;
 
 /* NumericsSamplingMode (runtime_policy.h:13-18). */
@@ -374,6 +378,13 @@ tmnn_status tmnn_cuda_get_numerics_stats(tmnn_ctx *ctx,
 /* Encoding only (parity instrument): features [n x L*F] f32, and when
  * non-NULL the first table index of every corner [n x L x 2^d] (u32) and the
  * base grid cell [n x L x d] (i32). Host pointers. */
+/* Morton order of a batch (parity instrument for morton_sort.h:60-110): perm
+ * [n] = input index of the i-th point after the device's stable sort on the
+ * top key_bits of the code (0: the whole code).  Host pointers. */
+tmnn_status tmnn_cuda_debug_morton_order(tmnn_ctx *ctx, const float *positions,
+                                         uint32_t n, int32_t key_bits,
+                                         uint32_t *perm);
+
 tmnn_status tmnn_cuda_debug_encode(tmnn_ctx *ctx, const float *positions,
                                    uint32_t n, float *features,
                                    uint32_t *corner_index, int32_t *cells);

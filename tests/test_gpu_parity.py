@@ -239,3 +239,25 @@ def test_errors_and_guards():
     tr.close()
     with pytest.raises(t.ClosedError):
         tr.step()
+
+
+@pytest.mark.parametrize("d", [3, 4])
+@pytest.mark.parametrize("key_bits", [0, 12, 8, 20])
+def test_morton_order_matches_stable_sort_of_reference_codes(d, key_bits):
+    """Device Morton permutation (morton_sort.h:60-110 codes): a stable sort
+    on the top key_bits of the code (counting sort for <= 12 bits, CUB radix
+    sort otherwise) equals numpy's stable argsort of the oracle's codes."""
+    kw = dict(L=4, F=2, log2T=10, d=d, W=64, H=1, O=1)
+    tr = cuda_trainer(**kw)
+    rng = np.random.default_rng(d * 100 + key_bits)
+    n = 70001
+    pos = rng.uniform(-1.05, 1.05, (n, d)).astype(np.float32)
+    pos[:1000] = pos[1000:2000]  # duplicate codes exercise stability
+    perm = tr.debug_morton_order(pos, key_bits)
+    f = o.lib.tmo_morton4 if d == 4 else o.lib.tmo_morton3
+    codes = np.array([f(*map(float, p)) for p in pos], np.uint64)
+    end = 32 if d == 4 else 30
+    shift = end - key_bits if 0 < key_bits < end else 0
+    want = np.argsort(codes >> np.uint64(shift), kind="stable")
+    assert np.array_equal(perm, want.astype(np.uint32))
+    tr.close()

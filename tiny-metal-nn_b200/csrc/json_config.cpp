@@ -388,7 +388,8 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
   const JVal &b2 = section("b200");
   known_keys(b2, {"family", "hash_grad_format", "table_dtype", "morton_sort",
                   "sparse_hash_adam", "active_levels", "numerics_sampling_mode",
-                  "numerics_sample_interval", "bad_step_recovery"},
+                  "numerics_sample_interval", "bad_step_recovery",
+                  "morton_key_bits"},
              "b200", d);
   const std::string fam = str(b2, "family", "Auto", "b200.family", d);
   if (fam == "Auto") cfg->family = TMNN_FAMILY_AUTO;
@@ -412,6 +413,12 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
     cfg->sparse_hash_adam =
         boolean(b2, "sparse_hash_adam", true, "b200.sparse_hash_adam", d) ? 1 : 0;
   cfg->active_levels = integer(b2, "active_levels", 0, "b200.active_levels", d);
+  if (b2.get("morton_key_bits")) {
+    const int kb = integer(b2, "morton_key_bits", 12, "b200.morton_key_bits", d);
+    if (kb < 0 || kb > 32)
+      d.err("b200.morton_key_bits", "must be in [0, 32]");
+    cfg->morton_key_bits = kb;
+  }
   // RuntimePolicyOverrides (include/tiny-metal-nn/runtime_policy.h:43-52):
   // the numerics guard knobs, with the enum names of the reference
   if (b2.get("numerics_sampling_mode")) {

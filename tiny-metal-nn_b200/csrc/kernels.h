@@ -55,7 +55,7 @@ size_t morton_temp_bytes(uint32_t N);
 void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
                          uint32_t *codes_alt, uint32_t *idx,
                          uint32_t *perm_out, void *temp, size_t temp_bytes,
-                         cudaStream_t st);
+                         cudaStream_t st, int key_bits = 0);
 void launch_gather_rows(const float *src, int width, const uint32_t *perm,
                         float *dst, uint32_t N, cudaStream_t st);
 void launch_scatter_rows(const float *src, int width, const uint32_t *perm,

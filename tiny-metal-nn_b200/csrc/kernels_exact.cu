@@ -6,6 +6,7 @@
 // path's reference-order variant, and the weight initialiser / optimizer of
 // every family.
 #include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -755,21 +756,89 @@ __device__ inline uint32_t quant(float v, float cells) {
   return (uint32_t)fminf(fmaxf(mapped, 0.0f), cells - 1.0f);
 }
 
-// morton_sort.h:14-58 codes; the permutation is sorted by CUB's stable radix
-// sort, so equal codes keep their input order.
+// morton_sort.h:14-58 codes.
+__device__ inline uint32_t morton_code(const float *p, int d) {
+  return d == 4 ? (expand4(quant(p[3], 256.f)) << 3) |
+                      (expand4(quant(p[2], 256.f)) << 2) |
+                      (expand4(quant(p[1], 256.f)) << 1) |
+                      expand4(quant(p[0], 256.f))
+                : (expand3(quant(p[2], 1024.f)) << 2) |
+                      (expand3(quant(p[1], 1024.f)) << 1) |
+                      expand3(quant(p[0], 1024.f));
+}
+
+// Codes and identity indices for CUB's stable radix sort (equal keys keep
+// their input order).
 __global__ void k_morton_codes(const float *__restrict__ pos, int d,
                                uint32_t *codes, uint32_t *idx, uint32_t N) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= N) return;
-  const float *p = pos + (size_t)i * d;
-  codes[i] = d == 4 ? (expand4(quant(p[3], 256.f)) << 3) |
-                          (expand4(quant(p[2], 256.f)) << 2) |
-                          (expand4(quant(p[1], 256.f)) << 1) |
-                          expand4(quant(p[0], 256.f))
-                    : (expand3(quant(p[2], 1024.f)) << 2) |
-                          (expand3(quant(p[1], 1024.f)) << 1) |
-                          expand3(quant(p[0], 1024.f));
+  codes[i] = morton_code(pos + (size_t)i * d, d);
   idx[i] = i;
+}
+
+// Stable counting sort on short keys (the top <= 12 bits of the code): the
+// same permutation as the stable radix sort, in three light passes.  Block b
+// owns points [b*chunk, (b+1)*chunk).
+constexpr int kCsBuckets = 4096;
+
+__global__ void __launch_bounds__(256)
+    k_count_hist(const float *__restrict__ pos, int d, uint32_t N,
+                 uint32_t chunk, int shift, int nbuckets, uint32_t *hist) {
+  __shared__ uint32_t cnt[kCsBuckets];
+  for (int k = threadIdx.x; k < nbuckets; k += blockDim.x) cnt[k] = 0;
+  __syncthreads();
+  const uint32_t b0 = blockIdx.x * chunk;
+  const uint32_t b1 = min(N, b0 + chunk);
+  for (uint32_t i = b0 + threadIdx.x; i < b1; i += blockDim.x)
+    atomicAdd(&cnt[morton_code(pos + (size_t)i * d, d) >> shift], 1u);
+  __syncthreads();
+  for (int k = threadIdx.x; k < nbuckets; k += blockDim.x)
+    hist[(size_t)k * gridDim.x + blockIdx.x] = cnt[k];
+}
+
+// offs = exclusive scan of hist in (bucket, block) order: the first sorted
+// slot of block b's points with key k.  Points are ranked 256 at a time;
+// within a round the eight warps take their ranks in warp order, each warp
+// grouping equal keys with __match_any_sync, so the order is stable.
+__global__ void __launch_bounds__(256)
+    k_count_scatter(const float *__restrict__ pos, int d, uint32_t N,
+                    uint32_t chunk, int shift, int nbuckets,
+                    const uint32_t *__restrict__ offs, uint32_t *perm) {
+  __shared__ uint32_t next[kCsBuckets];
+  for (int k = threadIdx.x; k < nbuckets; k += blockDim.x)
+    next[k] = offs[(size_t)k * gridDim.x + blockIdx.x];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t b0 = blockIdx.x * chunk;
+  const uint32_t b1 = min(N, b0 + chunk);
+  for (uint32_t base = b0; base < b1; base += blockDim.x) {
+    const uint32_t i = base + threadIdx.x;
+    const bool valid = i < b1;
+    const uint32_t key =
+        valid ? morton_code(pos + (size_t)i * d, d) >> shift : 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    const int leader = __ffs(peers) - 1;
+    const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+    for (int w = 0; w < 8; ++w) {
+      if (warp == w) {
+        uint32_t start = 0;
+        if (valid && lane == leader) {
+          start = next[key];
+          next[key] = start + __popc(peers);
+        }
+        start = __shfl_sync(0xffffffffu, start, leader);
+        if (valid) perm[start + rank] = i;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__host__ inline uint32_t count_chunk(uint32_t N) {
+  uint32_t c = (N + 295u) / 296u;  // at most 296 blocks (2 per SM)
+  c = (c + 255u) & ~255u;
+  return c < 2048u ? 2048u : c;
 }
 
 __global__ void k_gather_rows(const float *__restrict__ src, int width,
@@ -1352,7 +1421,12 @@ size_t morton_temp_bytes(uint32_t N) {
   cub::DeviceRadixSort::SortPairs(nullptr, bytes, (uint32_t *)nullptr,
                                   (uint32_t *)nullptr, (uint32_t *)nullptr,
                                   (uint32_t *)nullptr, (int)N, 0, 32);
-  return bytes;
+  const size_t nb = (N + count_chunk(N) - 1) / count_chunk(N);
+  const size_t hist = ((size_t)kCsBuckets * nb * 4 + 255) & ~(size_t)255;
+  size_t scan = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, scan, (uint32_t *)nullptr,
+                                (uint32_t *)nullptr, (int)(kCsBuckets * nb));
+  return bytes > hist + scan ? bytes : hist + scan;
 }
 
 // Sorted permutation of the batch by Morton code; returns perm (input index
@@ -1360,11 +1434,30 @@ size_t morton_temp_bytes(uint32_t N) {
 void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
                          uint32_t *codes_alt, uint32_t *idx,
                          uint32_t *perm_out, void *temp, size_t temp_bytes,
-                         cudaStream_t st) {
+                         cudaStream_t st, int key_bits) {
   if (N == 0) return;
+  const int end = d == 4 ? 32 : 30;
+  const int begin = key_bits > 0 && key_bits < end ? end - key_bits : 0;
+  if (end - begin <= 12) {
+    // short key: stable counting sort (the same permutation, fewer passes)
+    const uint32_t chunk = count_chunk(N);
+    const uint32_t nb = (N + chunk - 1) / chunk;
+    const int nbuckets = 1 << (end - begin);
+    uint32_t *hist = static_cast<uint32_t *>(temp);
+    const size_t hbytes = ((size_t)nbuckets * nb * 4 + 255) & ~(size_t)255;
+    size_t scan = temp_bytes - hbytes;
+    k_count_hist<<<nb, 256, 0, st>>>(pos, d, N, chunk, begin, nbuckets, hist);
+    cub::DeviceScan::ExclusiveSum(static_cast<uint8_t *>(temp) + hbytes, scan,
+                                  hist, hist, (int)(nbuckets * nb), st);
+    k_count_scatter<<<nb, 256, 0, st>>>(pos, d, N, chunk, begin, nbuckets,
+                                        hist, perm_out);
+    return;
+  }
   k_morton_codes<<<(N + 255) / 256, 256, 0, st>>>(pos, d, codes, idx, N);
+  // stable radix sort on the top key_bits of the code: points of one coarse
+  // Morton cell keep their input order
   cub::DeviceRadixSort::SortPairs(temp, temp_bytes, codes, codes_alt, idx,
-                                  perm_out, (int)N, 0, d == 4 ? 32 : 30, st);
+                                  perm_out, (int)N, begin, end, st);
 }
 
 void launch_gather_rows(const float *src, int width, const uint32_t *perm,

@@ -528,7 +528,8 @@ const float *stage_in(tmnn_ctx &c, const float *src, size_t count,
 void morton_sort(tmnn_ctx &c, const float *pos, const float *per_point,
                  uint32_t N, const float **pos_out, const float **pp_out) {
   launch_morton_order(pos, c.nd.d, N, c.codes.p, c.codes_alt.p, c.idx.p,
-                      c.perm.p, c.sort_tmp.p, c.sort_tmp.n, c.stream);
+                      c.perm.p, c.sort_tmp.p, c.sort_tmp.n, c.stream,
+                      c.cfg.morton_key_bits);
   launch_gather_rows(pos, c.nd.d, c.perm.p, c.pos_s.p, N, c.stream);
   c.launches += 3;
   *pos_out = c.pos_s.p;
@@ -1085,6 +1086,7 @@ void tmnn_cuda_default_train_cfg(tmnn_train_cfg *c) {
   c->numerics_sampling_mode = TMNN_NUMERICS_SAMPLED;
   c->numerics_sample_interval = 128;
   c->bad_step_recovery = TMNN_BAD_STEP_SIGNAL_ONLY;
+  c->morton_key_bits = 12;
   apply_policy_env(*c);
 }
 
@@ -1315,7 +1317,8 @@ tmnn_status tmnn_cuda_forward_backward_noalloc(tmnn_ctx *c,
     const float *p = positions, *t = targets;
     if (c->cfg.morton_sort && n > 1) {
       launch_morton_order(p, c->nd.d, n, codes, codes_alt, idx, perm, sort_tmp,
-                          kNoAllocSortTempBytes, c->stream);
+                          kNoAllocSortTempBytes, c->stream,
+                          c->cfg.morton_key_bits);
       launch_gather_rows(p, c->nd.d, perm, pos_s, n, c->stream);
       launch_gather_rows(t, c->nd.O, perm, tgt_s, n, c->stream);
       c->launches += 4;
@@ -1418,6 +1421,29 @@ tmnn_status tmnn_cuda_evaluate_with_gradient(tmnn_ctx *c,
   return guarded([&] {
     BusyGuard g(c);
     evaluate_with_gradient(*c, positions, outputs, gradients, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_debug_morton_order(tmnn_ctx *c, const float *positions,
+                                         uint32_t n, int32_t key_bits,
+                                         uint32_t *perm) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    if (n > 0 && (!positions || !perm))
+      throw std::invalid_argument("debug_morton_order: null arguments");
+    if (n == 0) return;
+    CK(cudaSetDevice(c->device));
+    ensure_batch(*c, n);
+    const float *p = stage_in(*c, positions, (size_t)n * c->nd.d, c->pos_in, 0);
+    launch_morton_order(p, c->nd.d, n, c->codes.p, c->codes_alt.p, c->idx.p,
+                        c->perm.p, c->sort_tmp.p, c->sort_tmp.n, c->stream,
+                        key_bits);
+    c->launches += 3;
+    CK(cudaMemcpyAsync(perm, c->perm.p, (size_t)n * 4, cudaMemcpyDeviceToHost,
+                       c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
   });
 }
 

@@ -491,6 +491,18 @@ class Trainer:
 
     inference_with_gradient = evaluate_with_gradient
 
+    def debug_morton_order(self, input, key_bits=0):
+        """Device Morton permutation of a host batch (parity instrument)."""
+        h = self._handle()
+        pp, n, flags, _k = _arg(input, "input", self.n_input)
+        if flags:
+            raise ValueError("debug_morton_order takes host arrays")
+        perm = np.zeros(n, np.uint32)
+        self._guarded(lambda: _check(lib.tmnn_cuda_debug_morton_order(
+            h, pp, n, key_bits, perm.ctypes.data_as(C.c_void_p)),
+            "debug_morton_order"))
+        return perm
+
     def debug_encode(self, input):
         """(features, corner_index, cells) of the encoding (host arrays)."""
         h = self._handle()

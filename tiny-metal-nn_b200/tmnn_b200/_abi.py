@@ -53,7 +53,8 @@ class TrainCfg(C.Structure):
                 ("numerics_sampling_mode", C.c_int32),
                 ("numerics_sample_interval", C.c_int32),
                 ("bad_step_recovery", C.c_int32),
-                ("reserved", C.c_int32 * 3)]
+                ("morton_key_bits", C.c_int32),
+                ("reserved", C.c_int32 * 2)]
 
 
 class StepResult(C.Structure):
@@ -133,6 +134,7 @@ _SIGS = [
     ("tmnn_cuda_evaluate", C.c_int, [P, P, P, u32, u32]),
     ("tmnn_cuda_evaluate_with_gradient", C.c_int, [P, P, P, P, u32, u32]),
     ("tmnn_cuda_get_numerics_stats", C.c_int, [P, C.POINTER(NumericsStats)]),
+    ("tmnn_cuda_debug_morton_order", C.c_int, [P, P, u32, C.c_int32, P]),
     ("tmnn_cuda_debug_encode", C.c_int, [P, P, u32, P, P, P]),
     ("tmnn_cuda_export_opt_state", C.c_int,
      [P, P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(u32)]),
