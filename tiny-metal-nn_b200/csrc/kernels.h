@@ -55,7 +55,13 @@ size_t morton_temp_bytes(uint32_t N);
 void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
                          uint32_t *codes_alt, uint32_t *idx,
                          uint32_t *perm_out, void *temp, size_t temp_bytes,
-                         cudaStream_t st, int key_bits = 0);
+                         cudaStream_t st, int key_bits = 0,
+                         float *pos_dst = nullptr, const float *rows = nullptr,
+                         int width = 0, float *rows_dst = nullptr,
+                         bool *gathered = nullptr);
+// (With pos_dst and a short key the sort also writes the sorted position rows
+// and, when rows_dst is given, the sorted rows of `rows`; *gathered reports
+// whether it did, otherwise the caller gathers by perm.)
 void launch_gather_rows(const float *src, int width, const uint32_t *perm,
                         float *dst, uint32_t N, cudaStream_t st);
 void launch_scatter_rows(const float *src, int width, const uint32_t *perm,

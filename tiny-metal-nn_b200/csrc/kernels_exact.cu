@@ -804,7 +804,9 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     k_count_scatter(const float *__restrict__ pos, int d, uint32_t N,
                     uint32_t chunk, int shift, int nbuckets,
-                    const uint32_t *__restrict__ offs, uint32_t *perm) {
+                    const uint32_t *__restrict__ offs, uint32_t *perm,
+                    float *pos_dst, const float *__restrict__ rows, int width,
+                    float *rows_dst) {
   __shared__ uint32_t next[kCsBuckets];
   for (int k = threadIdx.x; k < nbuckets; k += blockDim.x)
     next[k] = offs[(size_t)k * gridDim.x + blockIdx.x];
@@ -820,6 +822,7 @@ __global__ void __launch_bounds__(256)
     const uint32_t peers = __match_any_sync(0xffffffffu, key);
     const int leader = __ffs(peers) - 1;
     const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+    uint32_t dst = 0;
     for (int w = 0; w < 8; ++w) {
       if (warp == w) {
         uint32_t start = 0;
@@ -827,10 +830,19 @@ __global__ void __launch_bounds__(256)
           start = next[key];
           next[key] = start + __popc(peers);
         }
-        start = __shfl_sync(0xffffffffu, start, leader);
-        if (valid) perm[start + rank] = i;
+        dst = __shfl_sync(0xffffffffu, start, leader) + rank;
       }
       __syncthreads();
+    }
+    // the moves run outside the warp-ordered ranking
+    if (valid) {
+      perm[dst] = i;
+      if (pos_dst)
+        for (int a = 0; a < d; ++a)
+          pos_dst[(size_t)dst * d + a] = pos[(size_t)i * d + a];
+      if (rows_dst)
+        for (int a = 0; a < width; ++a)
+          rows_dst[(size_t)dst * width + a] = rows[(size_t)i * width + a];
     }
   }
 }
@@ -838,7 +850,7 @@ __global__ void __launch_bounds__(256)
 __host__ inline uint32_t count_chunk(uint32_t N) {
   uint32_t c = (N + 295u) / 296u;  // at most 296 blocks (2 per SM)
   c = (c + 255u) & ~255u;
-  return c < 2048u ? 2048u : c;
+  return c < 1024u ? 1024u : c;
 }
 
 __global__ void k_gather_rows(const float *__restrict__ src, int width,
@@ -1434,7 +1446,10 @@ size_t morton_temp_bytes(uint32_t N) {
 void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
                          uint32_t *codes_alt, uint32_t *idx,
                          uint32_t *perm_out, void *temp, size_t temp_bytes,
-                         cudaStream_t st, int key_bits) {
+                         cudaStream_t st, int key_bits, float *pos_dst,
+                         const float *rows, int width, float *rows_dst,
+                         bool *gathered) {
+  if (gathered) *gathered = false;
   if (N == 0) return;
   const int end = d == 4 ? 32 : 30;
   const int begin = key_bits > 0 && key_bits < end ? end - key_bits : 0;
@@ -1450,7 +1465,9 @@ void launch_morton_order(const float *pos, int d, uint32_t N, uint32_t *codes,
     cub::DeviceScan::ExclusiveSum(static_cast<uint8_t *>(temp) + hbytes, scan,
                                   hist, hist, (int)(nbuckets * nb), st);
     k_count_scatter<<<nb, 256, 0, st>>>(pos, d, N, chunk, begin, nbuckets,
-                                        hist, perm_out);
+                                        hist, perm_out, pos_dst, rows,
+                                        width, rows_dst);
+    if (gathered) *gathered = pos_dst != nullptr;
     return;
   }
   k_morton_codes<<<(N + 255) / 256, 256, 0, st>>>(pos, d, codes, idx, N);

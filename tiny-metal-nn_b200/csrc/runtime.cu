@@ -524,18 +524,26 @@ const float *stage_in(tmnn_ctx &c, const float *src, size_t count,
 }
 
 // Morton order of the batch (morton_sort.h:60-110) on the device: codes,
-// stable radix sort, then row gathers of positions and the per-point array.
+// stable sort (counting sort for short keys, which also moves the rows),
+// then row gathers of positions and the per-point array where needed.
 void morton_sort(tmnn_ctx &c, const float *pos, const float *per_point,
                  uint32_t N, const float **pos_out, const float **pp_out) {
+  bool gathered = false;
   launch_morton_order(pos, c.nd.d, N, c.codes.p, c.codes_alt.p, c.idx.p,
                       c.perm.p, c.sort_tmp.p, c.sort_tmp.n, c.stream,
-                      c.cfg.morton_key_bits);
-  launch_gather_rows(pos, c.nd.d, c.perm.p, c.pos_s.p, N, c.stream);
+                      c.cfg.morton_key_bits, c.pos_s.p, per_point, c.nd.O,
+                      per_point ? c.tgt_s.p : nullptr, &gathered);
   c.launches += 3;
   *pos_out = c.pos_s.p;
-  if (per_point) {
-    launch_gather_rows(per_point, c.nd.O, c.perm.p, c.tgt_s.p, N, c.stream);
+  if (!gathered) {
+    launch_gather_rows(pos, c.nd.d, c.perm.p, c.pos_s.p, N, c.stream);
     c.launches++;
+  }
+  if (per_point) {
+    if (!gathered) {
+      launch_gather_rows(per_point, c.nd.O, c.perm.p, c.tgt_s.p, N, c.stream);
+      c.launches++;
+    }
     *pp_out = c.tgt_s.p;
   }
 }
