@@ -662,6 +662,10 @@ def main():
     # device-resident points per call
     eg = None
     if w["O"] == 1:
+        if world > 1:
+            # the sharded optimizer leaves the fp32 master partial on each
+            # rank; the input gradient reads it (collective on every rank)
+            tr.dp_sync_state()
         gout = torch.empty((1 << 20, w["d"]), device="cuda")
         for _ in range(3):
             tr.evaluate_with_gradient(q, out=out, gradients=gout)
