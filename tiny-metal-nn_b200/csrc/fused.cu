@@ -50,7 +50,7 @@ struct Layout {
   uint32_t tail_src, tail_dst, tail_bytes;
   int stream_w;
   // activation tiles
-  uint32_t x, h[kMaxHidden], dh[2], dy, misc;
+  uint32_t x, h[kMaxHidden], dy, misc;
   uint32_t total;
   int xc, hc;                  // stored columns of X and H tiles
   int n_h_tiles;
@@ -107,11 +107,7 @@ Layout make_layout(const NetDims &nd, bool train, bool stream = false) {
     off = align128(off + kTile * L.hc * 2);
   }
   if (train) {
-    for (int k = 0; k < (H > 1 ? 2 : 1); ++k) {
-      L.dh[k] = off;
-      off = align128(off + kTile * W * 2);
-    }
-    if (H == 1) L.dh[1] = L.dh[0];  // no ping-pong without hidden layers
+    // the pre-activation gradients of layer k overwrite H_k in place
     L.dy = off;
     off = align128(off + kTile * kOutCols * 2);
   }
@@ -389,7 +385,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
 // Encode and scatter split the point's levels between the two in 8-column
 // chunks; epilogues split the columns; TMEM lane quarter = warp % 4.
 template <int D, int F, int W, bool HALF, bool TRAIN>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
     k_fused(const __grid_constant__ FusedParams P) {
   extern __shared__ __align__(128) uint8_t sm[];
   const NetDims &nd = P.nd;
@@ -571,7 +567,6 @@ __global__ void __launch_bounds__(kThreads)
     }
     publish();
     // ---- backward through the output layer
-    int cur = 0;
     if (t == 0) {
       tc::fence_after_sync();
       // dH = dY . Wout^T   (B = Wout stored [W x 16] as K-major rows N = j)
@@ -586,24 +581,25 @@ __global__ void __launch_bounds__(kThreads)
     sync_mma();
     if (!ok) break;
     for (int k = H - 1; k >= 0; --k) {
-      // dpre_k = D * relu'(H_k) -> dH[cur]
+      // dpre_k = D * relu'(H_k), written over H_k (each thread rewrites
+      // the elements it read; the MMAs that read H_k have completed, and its
+      // ones column is left alone)
       {
-        const __half *Hk = reinterpret_cast<const __half *>(sm + Ly.h[k]);
-        __half *dHt = reinterpret_cast<__half *>(sm + Ly.dh[cur]);
+        __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[k]);
         for (int c0 = half * 16; c0 < W; c0 += 32) {
           float v[16], hv[16];
           tc::tmem_ld16(T_s + lane_base + c0, v);
           load_row16(Hk, Ly.hc, r, c0, hv);
 #pragma unroll
           for (int i = 0; i < 16; ++i) v[i] = hv[i] > 0.f ? v[i] : 0.f;
-          store_row16(dHt, W, r, c0, v);
+          store_row16(Hk, Ly.hc, r, c0, v);
         }
       }
       publish();
       if (t == 0) {
         tc::fence_after_sync();
-        const tc::Operand dHk{sbase + Ly.dh[cur], W, 0};
-        const tc::Operand dHkT{sbase + Ly.dh[cur], W, 1};
+        const tc::Operand dHk{sbase + Ly.h[k], Ly.hc, 0};
+        const tc::Operand dHkT{sbase + Ly.h[k], Ly.hc, 1};
         if (k > 0) {
           tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.sw[k], W, 0}, kTile, W, W, 0);
           tc::gemm(tmem + Ly.t_dwk[k], dHkT,
@@ -618,7 +614,7 @@ __global__ void __launch_bounds__(kThreads)
       }
       sync_mma();
       if (!ok) break;
-      cur ^= 1;
+
     }
     if (!ok) break;
     first = false;
