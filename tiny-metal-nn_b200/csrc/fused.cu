@@ -1057,13 +1057,14 @@ uint32_t pipe_gcols(const NetDims &nd) {
   return (c + 31u) & ~31u;
 }
 
-// Tiles in flight: as many as TMEM holds, 2..4; 0 when the weights do not
+// Tiles in flight: as many as TMEM holds, 2..6; 0 when the weights do not
 // fit in shared memory.
 int pipe_groups(const NetDims &nd) {
   const Layout L = make_layout(nd, false);
   if (align128(L.image_bytes) + 128 > kPipeSmemMax) return 0;
   int ng = (int)(512 / pipe_gcols(nd));
-  if (ng > 4) ng = 4;
+  if (ng > 6) ng = 6;
+  if (nd.W >= 64 && ng > 4) ng = 4;  // measured: more tiles do not help there
   return ng >= 2 ? ng : 0;
 }
 
@@ -1097,7 +1098,8 @@ int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
 #define TMNN_PIPE(WW)                                      \
   case WW:                                                 \
     fn = NG == 2 ? k_mlp_pipe<WW, 2>                       \
-         : NG == 3 ? k_mlp_pipe<WW, 3> : k_mlp_pipe<WW, 4>; \
+         : NG == 3 ? k_mlp_pipe<WW, 3> : NG == 4 ? k_mlp_pipe<WW, 4> \
+         : NG == 5 ? k_mlp_pipe<WW, 5> : k_mlp_pipe<WW, 6>; \
     break;
   switch (nd.W) { TMNN_PIPE(16) TMNN_PIPE(32) TMNN_PIPE(64) TMNN_PIPE(128) }
 #undef TMNN_PIPE
