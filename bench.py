@@ -68,9 +68,11 @@ WORKLOADS = {
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample of the
 # dominant kernel, from the committed ncu capture of the same bench command
-# (profiles/fused_train_sdf3d.md: 162.2 MB per 2^18-point launch), per
-# workload and family; absent pairs report traffic null.
-NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 162.2e6 / (1 << 18)}
+# (profiles/fused_train_sdf3d.md: 178.4 MB per 2^18-point launch;
+# profiles/fused_train_field4d.md: 3.92 GB), per workload and family; absent
+# pairs report traffic null.
+NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 178.4e6 / (1 << 18),
+                          ("field4d", "FullyFused"): 3919.5e6 / (1 << 18)}
 
 
 def log(*a):
