@@ -381,11 +381,13 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// The CTA has 256 threads: thread t and t + 128 share point (row) t % 128.
-// Encode and scatter split the point's levels between the two in 8-column
-// chunks; epilogues split the columns; TMEM lane quarter = warp % 4.
-template <int D, int F, int W, bool HALF, bool TRAIN>
-__global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
+// The CTA has 128 * Q threads (Q = 2 or 4): threads t, t + 128, ... share
+// point (row) t % 128.  Encode and scatter split the point's levels among the
+// Q in 8-column chunks; epilogues split the columns; TMEM lane quarter =
+// warp % 4.  Q = 4 serves shapes whose TMEM budget allows only two CTAs per
+// SM, so that an SM still holds 32 warps to keep table accesses in flight.
+template <int D, int F, int W, bool HALF, bool TRAIN, int Q = 2>
+__global__ void __launch_bounds__(128 * Q, TRAIN ? 8 / Q : 1)
     k_fused(const __grid_constant__ FusedParams P) {
   extern __shared__ __align__(128) uint8_t sm[];
   const NetDims &nd = P.nd;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
   const int t = threadIdx.x;
   const int warp = t >> 5;
   const int r = t & (kTile - 1);   // point row in the tile
-  const int half = t >> 7;         // which half of the work on that row
+  const int half = t >> 7;         // which part of the work on that row
   const int In = nd.In, H = nd.H, O = nd.O;
   constexpr int LPC = 8 / F;       // levels per 8-column chunk
   constexpr int NL = D == 4 ? 1 : (LPC < 2 ? LPC : 2);  // levels per load batch
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
   {
     const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage + Ly.tail_src);
     uint4 *dst = reinterpret_cast<uint4 *>(sm + Ly.tail_dst);
-    for (uint32_t i = t; i < Ly.tail_bytes / 16; i += kThreads) dst[i] = src[i];
+    for (uint32_t i = t; i < Ly.tail_bytes / 16; i += 128 * Q) dst[i] = src[i];
     if (TRAIN && half == 0) {
       float ones[16] = {1.f};
       store_row16(X, Ly.xc, r, In, ones);
@@ -459,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
     }
     if constexpr (D == 0) {
       // plain MLP: the input features come from memory (fp16)
-      for (int ch = half; ch < n_chunks; ch += 2) {
+      for (int ch = half; ch < n_chunks; ch += Q) {
         uint4 u = make_uint4(0u, 0u, 0u, 0u);
         if (valid)
           u = __ldg(reinterpret_cast<const uint4 *>(P.xin + (size_t)row * In) + ch);
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
       }
     } else {
       // ---- encode: chunks of 8 feature columns, alternating between halves
-      for (int ch = half; ch < n_chunks; ch += 2) {
+      for (int ch = half; ch < n_chunks; ch += Q) {
         float acc[8];
 #pragma unroll
         for (int j = 0; j < LPC; j += NL)
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
         const uint32_t bytes = (uint32_t)(k == 0 ? In : W) * W * 2;
         const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage + Ly.w[k]);
         uint4 *dst = reinterpret_cast<uint4 *>(sm + Ly.sw[k]);
-        for (uint32_t i = t; i < bytes / 16; i += kThreads) dst[i] = src[i];
+        for (uint32_t i = t; i < bytes / 16; i += 128 * Q) dst[i] = src[i];
         publish();
       }
       if (t == 0) {
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
       if (!ok) break;
       const float *bk = reinterpret_cast<const float *>(sm + Ly.sb[k]);
       __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[hk]);
-      for (int c0 = half * 16; c0 < W; c0 += 32) {
+      for (int c0 = half * 16; c0 < W; c0 += 16 * Q) {
         float v[16];
         tc::tmem_ld16(T_s + lane_base + c0, v);
 #pragma unroll
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
       // ones column is left alone)
       {
         __half *Hk = reinterpret_cast<__half *>(sm + Ly.h[k]);
-        for (int c0 = half * 16; c0 < W; c0 += 32) {
+        for (int c0 = half * 16; c0 < W; c0 += 16 * Q) {
           float v[16], hv[16];
           tc::tmem_ld16(T_s + lane_base + c0, v);
           load_row16(Hk, Ly.hc, r, c0, hv);
@@ -621,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
     // ---- scatter d_feature * corner weight into the hash gradients
     if constexpr (D > 0) {
       const int levels = nd.active_levels;
-      for (int ch = half; ch < n_chunks; ch += 2) {
+      for (int ch = half; ch < n_chunks; ch += Q) {
         float df[8];
         tmem_ld8(T_s + lane_base + ch * 8, df);
         if (!valid) continue;
@@ -684,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
       // plain MLP: dL/dx to memory (unscaled fp32), for a caller that
       // back-propagates further (e.g. into the features of another network)
       if (P.dxout) {
-        for (int ch = half; ch < n_chunks; ch += 2) {
+        for (int ch = half; ch < n_chunks; ch += Q) {
           float df[8];
           tmem_ld8(T_s + lane_base + ch * 8, df);
           if (!valid) continue;
@@ -710,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, TRAIN ? 4 : 1)
     const int rr = W == 128 ? r : (warp & 3) * 16 + lane;
     const float s = P.inv_dscale;
     auto flush = [&](uint32_t tcol, int ncols, auto &&dest) {
-      for (int c0 = half * 16; c0 < ncols; c0 += 32) {
+      for (int c0 = half * 16; c0 < ncols; c0 += 16 * Q) {
         float v[16];
         tc::tmem_ld16(tmem + lane_base + tcol + c0, v);
         if (!has_row) continue;
@@ -1126,6 +1128,17 @@ KernelFn pick_w(int W) {
   return nullptr;
 }
 
+// Training kernels with four threads per point (Q = 4), for the common
+// width 64 with two features per level.
+KernelFn pick_train_q4(int d, int F, int W, bool half) {
+  if (F != 2 || W != 64) return nullptr;
+  if (d == 3) return half ? (KernelFn)k_fused<3, 2, 64, true, true, 4>
+                          : (KernelFn)k_fused<3, 2, 64, false, true, 4>;
+  if (d == 4) return half ? (KernelFn)k_fused<4, 2, 64, true, true, 4>
+                          : (KernelFn)k_fused<4, 2, 64, false, true, 4>;
+  return nullptr;
+}
+
 template <bool TRAIN>
 KernelFn pick(int d, int F, int W, bool half) {
 #define TMNN_PICK(DD, FF)                                                       \
@@ -1219,6 +1232,13 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   const bool half = spec.table_dtype == TMNN_DTYPE_F16 && table_h;
   KernelFn fn = train ? pick<true>(nd.d, nd.F, nd.W, half)
                       : pick<false>(nd.d, nd.F, nd.W, half);
+  int threads = kThreads;
+  if (train && 512 / Ly.tmem_cols <= 2) {
+    if (KernelFn f4 = pick_train_q4(nd.d, nd.F, nd.W, half)) {
+      fn = f4;
+      threads = 512;
+    }
+  }
   if (!fn) throw std::runtime_error("fused: no kernel for this shape");
   cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        (int)Ly.total);
@@ -1229,7 +1249,7 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor,
                          dev);
   int per_sm = smem_sm / (int)(Ly.total + 1024);
-  if (per_sm > 2048 / kThreads) per_sm = 2048 / kThreads;
+  if (per_sm > 2048 / threads) per_sm = 2048 / threads;
   const int tmem_fit = (int)(512 / Ly.tmem_cols);
   if (per_sm > tmem_fit) per_sm = tmem_fit;
   if (per_sm < 1) per_sm = 1;
@@ -1237,7 +1257,7 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
   uint32_t grid = (uint32_t)num_sms * per_sm;
   if (grid > P.ntiles) grid = P.ntiles;
   if (grid == 0) return launches;
-  fn<<<grid, kThreads, Ly.total, st>>>(P);
+  fn<<<grid, threads, Ly.total, st>>>(P);
   return launches + 1;
 }
 
