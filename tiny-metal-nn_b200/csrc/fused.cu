@@ -1050,7 +1050,7 @@ __global__ void __launch_bounds__(128 + 128 * NG)
 constexpr uint32_t kPipeSmemMax = 220 * 1024;
 
 int ensure_packed(FusedWorkspace &ws, const NetDims &nd, const float *params,
-                  cudaStream_t st);
+                  cudaStream_t st, bool train);
 
 // TMEM columns per tile: W fp32 accumulator columns + max(In, W)/2 columns
 // of fp16 pairs, rounded up to 32.
@@ -1078,7 +1078,7 @@ uint32_t pipe_smem(const NetDims &nd) {
 int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
                     const __half *x, float *out, uint32_t N, int num_sms,
                     cudaStream_t st, int out_act) {
-  int launches = ensure_packed(ws, nd, mlp, st);
+  int launches = ensure_packed(ws, nd, mlp, st, false);
   PipeParams P{};
   P.nd = nd;
   P.lay = make_layout(nd, false);
@@ -1185,33 +1185,39 @@ NetDims dims_of(const tmnn_spec &s) {
 
 // (Re)packs the training and inference weight images when the weights
 // changed; returns the kernels launched.
+// (Re)packs the training or the inference weight image (whichever the
+// caller is about to use) if the weights changed since it was last packed;
+// returns the kernels launched.
 int ensure_packed(FusedWorkspace &ws, const NetDims &nd, const float *params,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool train) {
   int launches = 0;
   if (!ws.err) {
     if (cudaMalloc(&ws.err, sizeof(int)) != cudaSuccess)
       throw std::runtime_error("fused: cudaMalloc failed");
     cudaMemsetAsync(ws.err, 0, sizeof(int), st);
   }
-  const Layout Ly = make_layout(nd, false);
-  if (ws.dirty || ws.wpack_bytes < 2ull * Ly.image_bytes) {
-    const Layout Lt = make_layout(nd, true), Lf = make_layout(nd, false);
-    const size_t need = (size_t)Lt.image_bytes + Lf.image_bytes;
-    if (ws.wpack_bytes < need) {
-      if (ws.wpack) cudaFree(ws.wpack);
-      if (cudaMalloc(&ws.wpack, need) != cudaSuccess)
-        throw std::runtime_error("fused: cudaMalloc failed");
-      ws.wpack_bytes = need;
-    }
-    cudaMemsetAsync(ws.wpack, 0, need, st);
+  const Layout Lt = make_layout(nd, true), Lf = make_layout(nd, false);
+  const size_t need = (size_t)Lt.image_bytes + Lf.image_bytes;
+  if (ws.wpack_bytes < need) {
+    if (ws.wpack) cudaFree(ws.wpack);
+    if (cudaMalloc(&ws.wpack, need) != cudaSuccess)
+      throw std::runtime_error("fused: cudaMalloc failed");
+    ws.wpack_bytes = need;
+    cudaMemsetAsync(ws.wpack, 0, need, st);  // alignment gaps stay zero
+    ws.dirty = ws.dirty_infer = true;
+  }
+  bool &dirty = train ? ws.dirty : ws.dirty_infer;
+  if (dirty) {
     const float *mlp = params + nd.hash_count;
     const int n = nd.W * nd.W > nd.In * nd.W ? nd.W * nd.W : nd.In * nd.W;
     const int grid = (n + 255) / 256 + 1;
-    k_pack<<<grid, 256, 0, st>>>(nd, Lt, mlp, (uint8_t *)ws.wpack);
-    k_pack<<<grid, 256, 0, st>>>(nd, Lf, mlp,
-                                 (uint8_t *)ws.wpack + Lt.image_bytes);
-    launches += 2;
-    ws.dirty = false;
+    if (train)
+      k_pack<<<grid, 256, 0, st>>>(nd, Lt, mlp, (uint8_t *)ws.wpack);
+    else
+      k_pack<<<grid, 256, 0, st>>>(nd, Lf, mlp,
+                                   (uint8_t *)ws.wpack + Lt.image_bytes);
+    launches += 1;
+    dirty = false;
   }
   return launches;
 }
@@ -1220,7 +1226,7 @@ int launch(FusedWorkspace &ws, const NetDims &nd, const tmnn_spec &spec,
            const float *params, const __half *table_h, bool train,
            FusedParams &P, int num_sms, cudaStream_t st) {
   const Layout Ly = make_layout(nd, train);
-  int launches = ensure_packed(ws, nd, params, st);
+  int launches = ensure_packed(ws, nd, params, st, train);
   P.nd = nd;
   P.lay = Ly;
   P.wimage = (const uint8_t *)ws.wpack +
@@ -1270,7 +1276,9 @@ bool fused_supported(const tmnn_spec &spec, const tmnn_train_cfg &cfg,
   return shape_ok(nd, true, why) && shape_ok(nd, false, why);
 }
 
-void fused_weights_changed(FusedWorkspace &ws) { ws.dirty = true; }
+void fused_weights_changed(FusedWorkspace &ws) {
+  ws.dirty = ws.dirty_infer = true;
+}
 
 void fused_release(FusedWorkspace &ws) {
   if (ws.wpack) cudaFree(ws.wpack);

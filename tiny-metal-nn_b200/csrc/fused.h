@@ -19,7 +19,8 @@ namespace tmnn {
 struct FusedWorkspace {
   void *wpack = nullptr;
   size_t wpack_bytes = 0;
-  bool dirty = true;
+  bool dirty = true;        // training image out of date
+  bool dirty_infer = true;  // inference image out of date
   int ctas_per_sm = 0;
   int *err = nullptr;
   bool no_pipe = false;  // plain-MLP inference: force the one-tile kernel

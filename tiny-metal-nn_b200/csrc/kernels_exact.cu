@@ -7,6 +7,7 @@
 // every family.
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
+#include <cub/block/block_radix_sort.cuh>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -798,59 +799,68 @@ __global__ void __launch_bounds__(256)
 }
 
 // offs = exclusive scan of hist in (bucket, block) order: the first sorted
-// slot of block b's points with key k.  Points are ranked 256 at a time;
-// within a round the eight warps take their ranks in warp order, each warp
-// grouping equal keys with __match_any_sync, so the order is stable.
-__global__ void __launch_bounds__(256)
+// slot of block b's points with key k.  The block sorts its chunk locally
+// (CUB's stable block radix sort on the key), so a point's slot is
+// offs[key][b] + its position among the block's points of that key; then
+// it moves its index, position row and per-point row there.
+constexpr int kCsThreads = 256, kCsItems = 8;
+
+__global__ void __launch_bounds__(kCsThreads)
     k_count_scatter(const float *__restrict__ pos, int d, uint32_t N,
                     uint32_t chunk, int shift, int nbuckets,
                     const uint32_t *__restrict__ offs, uint32_t *perm,
                     float *pos_dst, const float *__restrict__ rows, int width,
                     float *rows_dst) {
-  __shared__ uint32_t next[kCsBuckets];
-  for (int k = threadIdx.x; k < nbuckets; k += blockDim.x)
-    next[k] = offs[(size_t)k * gridDim.x + blockIdx.x];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  using BlockSort = cub::BlockRadixSort<uint32_t, kCsThreads, kCsItems, uint32_t>;
+  __shared__ union {
+    typename BlockSort::TempStorage sort;
+    uint32_t keys[kCsThreads * kCsItems];
+  } sh;
+  __shared__ uint32_t first[kCsBuckets];  // local sorted position of a key's
+                                          // first point (present keys only)
   const uint32_t b0 = blockIdx.x * chunk;
-  const uint32_t b1 = min(N, b0 + chunk);
-  for (uint32_t base = b0; base < b1; base += blockDim.x) {
-    const uint32_t i = base + threadIdx.x;
-    const bool valid = i < b1;
-    const uint32_t key =
-        valid ? morton_code(pos + (size_t)i * d, d) >> shift : 0xFFFFFFFFu;
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
-    const int leader = __ffs(peers) - 1;
-    const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
-    uint32_t dst = 0;
-    for (int w = 0; w < 8; ++w) {
-      if (warp == w) {
-        uint32_t start = 0;
-        if (valid && lane == leader) {
-          start = next[key];
-          next[key] = start + __popc(peers);
-        }
-        dst = __shfl_sync(0xffffffffu, start, leader) + rank;
-      }
-      __syncthreads();
-    }
-    // the moves run outside the warp-ordered ranking
-    if (valid) {
-      perm[dst] = i;
-      if (pos_dst)
-        for (int a = 0; a < d; ++a)
-          pos_dst[(size_t)dst * d + a] = pos[(size_t)i * d + a];
-      if (rows_dst)
-        for (int a = 0; a < width; ++a)
-          rows_dst[(size_t)dst * width + a] = rows[(size_t)i * width + a];
-    }
+  uint32_t key[kCsItems], idx[kCsItems];
+#pragma unroll
+  for (int j = 0; j < kCsItems; ++j) {
+    const uint32_t i = b0 + threadIdx.x * kCsItems + j;
+    idx[j] = i;
+    // points past the end sort last under the sentinel key nbuckets
+    key[j] = i < N ? morton_code(pos + (size_t)i * d, d) >> shift
+                   : (uint32_t)nbuckets;
+  }
+  int bits = 1;
+  while ((1 << bits) <= nbuckets) ++bits;
+  BlockSort(sh.sort).Sort(key, idx, 0, bits);  // stable, blocked result
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kCsItems; ++j) sh.keys[threadIdx.x * kCsItems + j] = key[j];
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kCsItems; ++j) {
+    const int p = threadIdx.x * kCsItems + j;
+    if (key[j] < (uint32_t)nbuckets && (p == 0 || sh.keys[p - 1] != key[j]))
+      first[key[j]] = (uint32_t)p;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kCsItems; ++j) {
+    if (key[j] >= (uint32_t)nbuckets) continue;
+    const int p = threadIdx.x * kCsItems + j;
+    const uint32_t dst =
+        offs[(size_t)key[j] * gridDim.x + blockIdx.x] + (uint32_t)p - first[key[j]];
+    const uint32_t i = idx[j];
+    perm[dst] = i;
+    if (pos_dst)
+      for (int a = 0; a < d; ++a)
+        pos_dst[(size_t)dst * d + a] = pos[(size_t)i * d + a];
+    if (rows_dst)
+      for (int a = 0; a < width; ++a)
+        rows_dst[(size_t)dst * width + a] = rows[(size_t)i * width + a];
   }
 }
 
-__host__ inline uint32_t count_chunk(uint32_t N) {
-  uint32_t c = (N + 295u) / 296u;  // at most 296 blocks (2 per SM)
-  c = (c + 255u) & ~255u;
-  return c < 1024u ? 1024u : c;
+__host__ inline uint32_t count_chunk(uint32_t) {
+  return (uint32_t)(kCsThreads * kCsItems);  // one block sort per chunk
 }
 
 __global__ void k_gather_rows(const float *__restrict__ src, int width,
