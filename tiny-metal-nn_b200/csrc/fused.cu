@@ -37,6 +37,11 @@ constexpr int kTile = 128;
 constexpr int kThreads = 256;
 constexpr int kMaxTrainHidden = 4;
 constexpr int kOutCols = 16;  // output layer padded to N = 16
+// Levels whose resolution is at most this are scattered with warp
+// aggregation (coarse grids: many points of a Morton-sorted warp share
+// corners there).
+constexpr float kAggMaxRes = 48.0f;
+constexpr uint32_t kAggBytes = 16 * 32 * 2 * 4;  // 16 warps x 32 lanes x 2 floats
 constexpr uint32_t kWaitBound = 1u << 26;
 
 struct Layout {
@@ -50,7 +55,7 @@ struct Layout {
   uint32_t tail_src, tail_dst, tail_bytes;
   int stream_w;
   // activation tiles
-  uint32_t x, h[kMaxHidden], dy, misc;
+  uint32_t x, h[kMaxHidden], dy, agg, misc;
   uint32_t total;
   int xc, hc;                  // stored columns of X and H tiles
   int n_h_tiles;
@@ -110,6 +115,8 @@ Layout make_layout(const NetDims &nd, bool train, bool stream = false) {
     // the pre-activation gradients of layer k overwrite H_k in place
     L.dy = off;
     off = align128(off + kTile * kOutCols * 2);
+    L.agg = off;  // per-warp staging of the warp-aggregated scatter
+    off = align128(off + kAggBytes);
   }
   L.misc = off;
   off = align128(off + 256);
@@ -623,9 +630,12 @@ __global__ void __launch_bounds__(128 * Q, TRAIN ? 8 / Q : 1)
     // ---- scatter d_feature * corner weight into the hash gradients
     if constexpr (D > 0) {
       const int levels = nd.active_levels;
+      const int lane = t & 31;
+      float *sa = reinterpret_cast<float *>(sm + Ly.agg) + warp * 64;
       for (int ch = half; ch < n_chunks; ch += Q) {
         float df[8];
         tmem_ld8(T_s + lane_base + ch * 8, df);
+        const unsigned vmask = __ballot_sync(0xffffffffu, valid);
         if (!valid) continue;
 #pragma unroll
         for (int j = 0; j < LPC; ++j) {
@@ -664,7 +674,25 @@ __global__ void __launch_bounds__(128 * Q, TRAIN ? 8 / Q : 1)
                 for (int q = 0; q < F; ++q)
                   gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(0x00800000);
               }
-              if (F == 2)
+              if (F == 2 && nd.res[l] <= kAggMaxRes) {
+                // warp aggregation: lanes with the same corner hand their
+                // contributions to the lowest such lane, which issues one
+                // reduction for the group
+                const unsigned peers = __match_any_sync(vmask, off);
+                sa[2 * lane] = gv[0];
+                sa[2 * lane + 1] = gv[F - 1];
+                __syncwarp(vmask);
+                if (lane == __ffs(peers) - 1) {
+                  float a = 0.f, b = 0.f;
+                  for (unsigned m = peers; m; m &= m - 1) {
+                    const int s = __ffs(m) - 1;
+                    a += sa[2 * s];
+                    b += sa[2 * s + 1];
+                  }
+                  red_add_f32x2(P.gh_float + off, a, b);
+                }
+                __syncwarp(vmask);
+              } else if (F == 2)
                 red_add_f32x2(P.gh_float + off, gv[0], gv[F - 1]);
               else if (F == 4)
                 red_add_f32x4(P.gh_float + off, gv[0], gv[1 % F], gv[2 % F],
