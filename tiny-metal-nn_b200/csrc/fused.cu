@@ -40,7 +40,7 @@ constexpr int kOutCols = 16;  // output layer padded to N = 16
 // Levels whose resolution is at most this are scattered with warp
 // aggregation (coarse grids: many points of a Morton-sorted warp share
 // corners there).
-constexpr float kAggMaxRes = 48.0f;
+constexpr float kAggMaxRes = 24.0f;
 constexpr uint32_t kAggBytes = 16 * 32 * 2 * 4;  // 16 warps x 32 lanes x 2 floats
 constexpr uint32_t kWaitBound = 1u << 26;
 
