@@ -442,13 +442,32 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
   }
 }
 
+// MLP part (a.mlp_count weights at w + a.hash_count, gradients gm), one
+// element per thread of the grid; same arithmetic as k_adam.
+__device__ inline void adam_mlp_range(const AdamArgs &a, float *w, float *m,
+                                      float *v, float *gm, bool veto) {
+  for (uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+       j < a.mlp_count; j += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t e = a.hash_count + j;
+    const float g = gm[j];
+    gm[j] = 0.0f;
+    if (veto) continue;
+    float wv = w[e], mv = m[e], vv = v[e];
+    adam_elem(wv, mv, vv, g, a.lr_mlp, a, a.l2_mlp, true);
+    w[e] = wv;
+    m[e] = mv;
+    v[e] = vv;
+  }
+}
+
 // Hash part of the same update, four elements per thread with 16-byte
-// accesses (the table size L*T*F is a multiple of 4).  Same arithmetic per
-// element as k_adam.
+// accesses (the table size L*T*F is a multiple of 4), followed by the MLP
+// weights (gm non-null) in the same launch.  Same arithmetic per element as
+// k_adam.
 __global__ void __launch_bounds__(256)
     k_adam_hash4(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
                  float *__restrict__ v, int32_t *gh_fixed, float *gh_float,
-                 uint8_t *__restrict__ touched, __half *table_h) {
+                 uint8_t *__restrict__ touched, __half *table_h, float *gm) {
   const uint64_t n4 = a.hash_count / 4;
   if (adam_vetoed(a)) {
     // the numerics guard rejected the step: only reset gradients and marks
@@ -465,6 +484,7 @@ __global__ void __launch_bounds__(256)
       else
         reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    if (gm) adam_mlp_range(a, w, m, v, gm, true);
     return;
   }
   for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
@@ -529,6 +549,7 @@ __global__ void __launch_bounds__(256)
       reinterpret_cast<uint2 *>(table_h)[q] = *reinterpret_cast<uint2 *>(h);
     }
   }
+  if (gm) adam_mlp_range(a, w, m, v, gm, false);
 }
 
 // ------------------------------------------------------------ numerics probe
@@ -1388,9 +1409,13 @@ void launch_adam(const AdamArgs &a, float *w, float *m, float *v,
   uint64_t blocks = (n4 + 255) / 256;
   const uint64_t cap = (uint64_t)num_sms * 64;
   if (blocks > cap) blocks = cap;
-  if (blocks)
+  if (blocks) {
+    // the MLP weights ride along in the same launch
     k_adam_hash4<<<(unsigned)blocks, 256, 0, st>>>(a, w, m, v, gh_fixed,
-                                                   gh_float, touched, table_h);
+                                                   gh_float, touched, table_h,
+                                                   a.mlp_count ? gm : nullptr);
+    return;
+  }
   // MLP weights: one thread each (slots = 0 selects the MLP range)
   AdamArgs am = a;
   am.slots = 0;

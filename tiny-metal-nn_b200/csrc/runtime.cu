@@ -638,7 +638,7 @@ void adam(tmnn_ctx &c, const StepStats *guard = nullptr) {
   a.guard = guard;
   launch_adam(a, c.params.p, c.m.p, c.v.p, c.gh_fixed.p, c.gh_float.p, c.gm.p,
               c.touched.p, c.table_h.p, c.num_sms, c.stream);
-  c.launches += 2;
+  c.launches += 1;
   fused_weights_changed(c.fws);
   if (!c.sparse)  // the dense path leaves the touched map unused
     CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
