@@ -1159,6 +1159,7 @@ KernelFn pick_w(int W) {
 // Training kernels with four threads per point (Q = 4), for the common
 // width 64 with two features per level.
 KernelFn pick_train_q4(int d, int F, int W, bool half) {
+  if (d == 0 && W == 64) return (KernelFn)k_fused<0, 2, 64, false, true, 4>;
   if (F != 2 || W != 64) return nullptr;
   if (d == 3) return half ? (KernelFn)k_fused<3, 2, 64, true, true, 4>
                           : (KernelFn)k_fused<3, 2, 64, false, true, 4>;
