@@ -394,7 +394,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
 // warp % 4.  Q = 4 serves shapes whose TMEM budget allows only two CTAs per
 // SM, so that an SM still holds 32 warps to keep table accesses in flight.
 template <int D, int F, int W, bool HALF, bool TRAIN, int Q = 2>
-__global__ void __launch_bounds__(128 * Q, TRAIN ? 8 / Q : 1)
+__global__ void __launch_bounds__(128 * Q, 8 / Q)
     k_fused(const __grid_constant__ FusedParams P) {
   extern __shared__ __align__(128) uint8_t sm[];
   const NetDims &nd = P.nd;
