@@ -96,6 +96,7 @@ def _create(cfg_json, n_in=3, n_out=1):
     ('{"encoding": ', "json:"),
     ('{"b200": {"bad_step_recovery": "Retry"}}', "allowed: SignalOnly, Throw"),
     ('{"b200": {"numerics_sampling_mode": "Often"}}', "allowed: Sampled"),
+    ('{"b200": {"morton_key_bits": 40}}', "b200.morton_key_bits: must be in [0, 32]"),
 ])
 def test_config_errors_reported_without_gpu(cfg, frag):
     st, msg, _ = _create(cfg)
