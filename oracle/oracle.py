@@ -286,8 +286,13 @@ class OracleTrainer:
 
     def __init__(self, s, hash_w, mlp_w, lr_hash=1e-2, lr_mlp=1e-3,
                  beta1=0.9, beta2=0.99, eps=1e-15, l1=0.0, l2=0.0,
-                 morton=True, nthreads=1):
+                 morton=True, nthreads=1, table_fp16=False):
         self.s = s
+        # table_fp16: the encode reads an fp16 copy of the table (the
+        # FullyFused family's gather copy with table_dtype F16), rounded to
+        # nearest-even from the fp32 master after every update; Adam still
+        # updates the fp32 master
+        self.table_fp16 = table_fp16
         self.w = np.concatenate([hash_w, mlp_w]).astype(np.float32)
         self.m = np.zeros_like(self.w)
         self.v = np.zeros_like(self.w)
@@ -315,6 +320,11 @@ class OracleTrainer:
             pos, tgt = pos[perm], tgt[perm]
         g = zero_grads(self.s)
         table, mlp = self.w[:self.hc].copy(), self.w[self.hc:].copy()
+        if self.table_fp16:
+            table = table.astype(np.float16).astype(np.float32)
+        if self.s.fp16_operands:
+            # the tensor-core kernel's dL/dy scale follows the batch size
+            self.s.dscale = pow2_scale(max(pos.shape[0], 1))
         if self.nthreads == 1:
             loss, g, _ = fwd_bwd(self.s, table, mlp, pos, tgt, grads=g)
         else:

@@ -1,7 +1,7 @@
 // Runs the reference's own MSL generator (tmnn::KernelCompiler /
 // MLPKernelEmitter, compiled from the reference sources) and prints the
 // kernel text for one spec.  Test infrastructure: its output is compiled as
-// C++ by oracle/ref_build.sh through oracle/ref/metal_shim.h.
+// C++ by oracle/ref_build.py through oracle/ref/metal_shim.h.
 //
 // usage: gen_msl ROLE L F log2T d W H O loss base scale huber active_mask
 //   ROLE: train | eval | fwd | extgrad | evalgrad

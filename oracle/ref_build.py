@@ -25,7 +25,22 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 REF = os.environ.get("TMNN_REFERENCE_ROOT", "/root/reference")
-NLOHMANN = "/opt/prime-rl/.venv/lib/python3.12/site-packages/include/cudnn_frontend/thirdparty"
+def _find_nlohmann():
+    """Directory holding nlohmann/json.hpp: TMNN_NLOHMANN_INCLUDE, else the
+    copy cudnn-frontend vendors in the Python environment, else the system
+    include path."""
+    env = os.environ.get("TMNN_NLOHMANN_INCLUDE")
+    if env:
+        return env
+    import sysconfig
+    for base in {sysconfig.get_paths()["purelib"], sysconfig.get_paths()["platlib"]}:
+        cand = os.path.join(base, "include", "cudnn_frontend", "thirdparty")
+        if os.path.exists(os.path.join(cand, "nlohmann", "json.hpp")):
+            return cand
+    return "/usr/include"
+
+
+NLOHMANN = _find_nlohmann()
 CXX = ["g++", "-std=c++23", "-O2", "-fPIC", "-ffp-contract=off",
        "-Wno-attributes", "-w"]
 

@@ -1,0 +1,225 @@
+"""Parity of the configuration that bench.py measures, at BASELINE sizes.
+
+The benchmarked path is the FullyFused family with the fp16 gather copy of
+the table (table_dtype F16), float hash gradients with implicit touch marks
+(a slot whose float gradient sum is nonzero counts as touched), the sparse
+Adam kernel that rewrites the fp16 copy in the same pass, and the 12-bit
+Morton sort.  These tests run exactly that, on the BASELINE tables:
+
+  sdf3d    3D, L=16 F=2, fp16 table, log2T=19, W=64 H=1 O=1, L1
+  image    (x, y, 0), L=16 F=2, fp32 table, log2T=15, W=64 H=2 O=3, L2
+  field4d  4D, L=16 F=2, fp16 table, log2T=22, W=64 H=2 O=4, L2
+
+on batches of 2^16 points (the oracle finishes a step in about a second),
+and check against the CPU oracle:
+
+  * first-step gradients, loss, outputs and the touched set: against the
+    oracle mode that rounds matrix operands to fp16 where the kernel does
+    (2e-3, kernel logic) and against the fp32 oracle (1e-2, the contract);
+  * one Adam step through the split API (forward_backward, adam_step): the
+    oracle's Adam (pinned bit-exact to the reference's MSL) applied to the
+    kernel's own gradients must reproduce the fp32 master, m and v bit for
+    bit, and the fp16 gather copy must equal the new master rounded to fp16
+    (the refresh inside the Adam kernel);
+  * five training steps: per-step losses within 1e-2 of the fp16-emulating
+    oracle trainer; the weight changes point the same way (cosine >= 0.99:
+    Adam moves every touched slot by about lr whatever the gradient's size,
+    so a slot whose gradient is within rounding of zero can move either way
+    and a norm of differences is the wrong measure);
+  * a 300-step loss curve on the full sdf3d table within 2 % of the oracle.
+
+Reference semantics: scatter mlp_kernel_emitter.cpp:672-901, sparse Adam
+include/tiny-metal-nn/kernels/adam_kernel_msl.h:120-203 and
+default_trainer.cpp:1868-1876.
+"""
+import numpy as np
+import pytest
+
+import oracle as o
+from _util import cuda_trainer, oracle_spec
+
+pytestmark = pytest.mark.gpu
+
+N = 1 << 16
+
+CONFIGS = {
+    "sdf3d": (dict(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=1,
+                   base=16.0, scale=1.447), "F16"),
+    "image": (dict(L=16, F=2, log2T=15, d=3, W=64, H=2, O=3, loss=0,
+                   base=16.0, scale=1.5), "F32"),
+    "field4d": (dict(L=16, F=2, log2T=22, d=4, W=64, H=2, O=4, loss=0,
+                     base=8.0, scale=1.5), "F16"),
+}
+
+
+def make_batch(name, n, seed):
+    """Seeded synthetic batches with the BASELINE shapes: SDF of 8 spheres,
+    RGB of 32 sinusoids on (x, y, 0), sum of 64 4D Gaussians."""
+    rng = np.random.default_rng(seed)
+    if name == "sdf3d":
+        pos = rng.uniform(-1, 1, (n, 3)).astype(np.float32)
+        g = np.random.default_rng(1234)
+        c = g.uniform(-0.6, 0.6, (8, 3)).astype(np.float32)
+        r = g.uniform(0.1, 0.4, 8).astype(np.float32)
+        dist = np.linalg.norm(pos[:, None, :] - c[None], axis=2) - r[None]
+        return pos, dist.min(axis=1, keepdims=True).astype(np.float32)
+    if name == "image":
+        xy = rng.uniform(0, 1, (n, 2)).astype(np.float32)
+        pos = np.concatenate([xy, np.zeros((n, 1), np.float32)], 1)
+        fr = np.random.default_rng(77).normal(size=(32, 2, 3)) * 6
+        ph = np.random.default_rng(78).uniform(0, 6.28, (32, 3))
+        tgt = np.zeros((n, 3), np.float32)
+        for k in range(32):
+            tgt += np.sin(xy @ fr[k] + ph[k]).astype(np.float32) / 32
+        return pos, tgt
+    pos = rng.uniform(0, 1, (n, 4)).astype(np.float32)
+    mu = np.random.default_rng(99).uniform(0, 1, (64, 4))
+    tgt = np.zeros((n, 4), np.float32)
+    for k in range(64):
+        tgt[:, k % 4] += np.exp(-((pos - mu[k]) ** 2).sum(1) * 20).astype(np.float32)
+    return pos, tgt
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def cosine(a, b):
+    a = a.astype(np.float64)
+    b = b.astype(np.float64)
+    return float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300))
+
+
+def trainer(name):
+    kw, table = CONFIGS[name]
+    tr = cuda_trainer(**kw, family="FullyFused", grad="F32", table=table,
+                      morton=True, lr_enc=1e-2, lr_net=1e-2, batch=N)
+    plan = tr.plan()
+    assert plan["family"] == "FullyFused", plan
+    return tr, kw, table
+
+
+def gather_table(hw, table):
+    return hw.astype(np.float16).astype(np.float32) if table == "F16" else hw
+
+
+def emulating(kw, n):
+    s = oracle_spec(**kw, grad="F32")
+    s.fp16_operands = 1
+    s.dscale = o.pow2_scale(n)
+    return s
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_first_step_gradients_at_baseline_size(name):
+    tr, kw, table = trainer(name)
+    hw, mw = tr.weights()
+    ht = gather_table(hw, table)
+    pos, tgt = make_batch(name, N, seed=11)
+    lsum = tr.forward_backward(pos, tgt)
+    gh, gm, touched = tr.read_buffer(3), tr.read_buffer(4), tr.read_buffer(21)
+    # kernel logic: fp16 operands where the kernel rounds them
+    ge = o.zero_grads(emulating(kw, N))
+    le = o.fwd_bwd_par(emulating(kw, N), ht, mw, pos, tgt, ge)
+    assert abs(lsum - le) <= 1e-3 * abs(le), (lsum, le)
+    assert rel(gh, ge["hash_float"]) <= 2e-3
+    assert rel(gm, ge["mlp"]) <= 2e-3
+    assert np.array_equal(touched, ge["touched"]), \
+        int(np.sum(touched != ge["touched"]))
+    # the contract: fp32 reference math at 1e-2
+    s32 = oracle_spec(**kw, grad="F32")
+    g32 = o.zero_grads(s32)
+    l32 = o.fwd_bwd_par(s32, ht, mw, pos, tgt, g32)
+    assert abs(lsum - l32) <= 1e-2 * abs(l32)
+    assert rel(gh, g32["hash_float"]) <= 1e-2
+    assert rel(gm, g32["mlp"]) <= 1e-2
+    out = tr.inference(pos[:8192])
+    ref = o.forward(s32, ht, mw, pos[:8192])
+    assert np.abs(out - ref).max() <= 1e-2 * max(np.abs(ref).max(), 1e-3)
+    tr.close()
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_adam_step_at_baseline_size_is_bit_exact(name):
+    """k_adam_hash4 with implicit touch and the fp16 refresh, at full table
+    size: the oracle's Adam on the kernel's own gradients gives the same
+    bits, and the gather copy is the new master rounded to fp16."""
+    tr, kw, table = trainer(name)
+    pos, tgt = make_batch(name, N, seed=12)
+    tr.training_step(pos, tgt)          # step 0: moments become nonzero
+    tr.zero_gradients()
+    pos, tgt = make_batch(name, N, seed=13)
+    tr.forward_backward(pos, tgt)
+    step = tr.step
+    w0 = np.concatenate(tr.weights())
+    m0, v0 = tr.read_buffer(8), tr.read_buffer(9)
+    gh, gm, touched = tr.read_buffer(3), tr.read_buffer(4), tr.read_buffer(21)
+    assert touched.any()
+    tr.adam_step()
+    w1 = np.concatenate(tr.weights())
+    m1, v1 = tr.read_buffer(8), tr.read_buffer(9)
+    s = oracle_spec(**kw, grad="F32")
+    wr, mr, vr = w0.copy(), m0.copy(), v0.copy()
+    o.adam(s, wr, mr, vr, {"hash_float": gh, "mlp": gm, "touched": touched},
+           step, lr_hash=1e-2, lr_mlp=1e-2)
+    hc = tr.hash_count
+    assert np.array_equal(w1[:hc].view(np.uint32), wr[:hc].view(np.uint32))
+    assert np.array_equal(m1[:hc].view(np.uint32), mr[:hc].view(np.uint32))
+    assert np.array_equal(v1[:hc].view(np.uint32), vr[:hc].view(np.uint32))
+    assert np.abs(w1[hc:] - wr[hc:]).max() <= 1e-6 * max(np.abs(wr[hc:]).max(), 1.0)
+    # untouched slots keep w, m, v
+    pairs = np.repeat(touched == 0, 2)
+    assert np.array_equal(w1[:hc][pairs], w0[:hc][pairs])
+    if table == "F16":
+        gather = tr.read_buffer(20)
+        assert np.array_equal(gather.view(np.uint16),
+                              w1[:hc].astype(np.float16).view(np.uint16))
+    # the gradients were cleared for the next step
+    assert not tr.read_buffer(3).any()
+    assert not tr.read_buffer(4).any()
+    tr.close()
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_five_training_steps_at_baseline_size(name):
+    tr, kw, table = trainer(name)
+    hw0, mw0 = tr.weights()
+    ot = o.OracleTrainer(emulating(kw, N), hw0, mw0, lr_hash=1e-2,
+                         lr_mlp=1e-2, nthreads=0, table_fp16=table == "F16")
+    for s in range(5):
+        pos, tgt = make_batch(name, N, seed=100 + s)
+        la = tr.training_step(pos, tgt)
+        lb = ot.training_step(pos, tgt)
+        assert abs(la - lb) <= 1e-2 * abs(lb), (s, la, lb)
+    hw, mw = tr.weights()
+    assert cosine(hw - hw0, ot.hash_w - hw0) >= 0.99
+    assert cosine(mw - mw0, ot.mlp_w - mw0) >= 0.99
+    # the same slots moved
+    moved_a = (hw != hw0).reshape(-1, 2).any(1)
+    moved_b = (ot.hash_w != hw0).reshape(-1, 2).any(1)
+    assert np.mean(moved_a != moved_b) <= 1e-4
+    if table == "F16":
+        gather = tr.read_buffer(20)
+        assert np.array_equal(gather.view(np.uint16),
+                              hw.astype(np.float16).view(np.uint16))
+    tr.close()
+
+
+@pytest.mark.slow
+def test_sdf3d_loss_curve_within_2_percent_full_table():
+    """300 steps of batch 2^16 on the full sdf3d table (fp16 gather copy,
+    float gradients, implicit touch, 12-bit Morton sort) against the fp32
+    CPU oracle trainer: the mean loss of the last 50 steps agrees to 2 %."""
+    tr, kw, table = trainer("sdf3d")
+    hw0, mw0 = tr.weights()
+    ot = o.OracleTrainer(oracle_spec(**kw, grad="F32"), hw0, mw0,
+                         lr_hash=1e-2, lr_mlp=1e-2, nthreads=0)
+    la, lb = [], []
+    for s in range(300):
+        pos, tgt = make_batch("sdf3d", N, seed=5000 + s)
+        la.append(tr.training_step(pos, tgt))
+        lb.append(ot.training_step(pos, tgt))
+    a, b = np.mean(la[-50:]), np.mean(lb[-50:])
+    assert abs(a - b) <= 0.02 * b, (a, b)
+    assert a < 0.5 * np.mean(la[:5])
+    tr.close()

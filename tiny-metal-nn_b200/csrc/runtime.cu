@@ -946,6 +946,12 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
       }
       activate_safe_family(c);
       c.step = done;  // the vetoed update is re-done with the same step
+      // Under the sharded optimizer the fp32 master outside this rank's
+      // shard is out of date (only the fp16 gather copy was all-gathered),
+      // and the SafeDebug kernels read the fp32 master: gather it first.
+      // Every rank reaches this point together (the anomaly decision is
+      // combined over the ranks), so the collective is matched.
+      if (c.stale) dp_sync_state(c);
       run_step(c, p, t, N, inv_N, prof, true, true);
       rep = read_report(c, global_n);
       anomaly = rep.anomaly();
