@@ -67,12 +67,15 @@ WORKLOADS = {
 }
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per sample of the
-# dominant kernel, from the committed ncu capture of the same bench command
-# (profiles/fused_train_sdf3d.md: 178.4 MB per 2^18-point launch;
-# profiles/fused_train_field4d.md: 3.92 GB), per workload and family; absent
-# pairs report traffic null.
-NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 178.4e6 / (1 << 18),
-                          ("field4d", "FullyFused"): 3919.5e6 / (1 << 18)}
+# dominant kernel, from one ncu capture of the same bench command (one k_fused
+# launch, --clock-control none), per workload and family; absent pairs report
+# traffic null.
+NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 187.64e6 / (1 << 18),
+                          ("field4d", "FullyFused"): 3753.30e6 / (1 << 18)}
+# L2 side of the same captures: lts__t_bytes.sum per sample and
+# lts__throughput.avg.pct_of_peak_sustained_elapsed of that launch.
+NCU_L2 = {("sdf3d", "FullyFused"): (2373.08e6 / (1 << 18), 59.92),
+          ("field4d", "FullyFused"): (8279.80e6 / (1 << 18), 34.19)}
 
 
 def log(*a):
@@ -211,6 +214,228 @@ def max_over_ranks(x, world):
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def hbm_peak():
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs")
+    return (hbm, "measured") if hbm else (6650.0, "fallback")
+
+
+def time_training(t, name, args, rank, world, local, steps, warmup,
+                  phase_steps, clocks=False):
+    """Trains workload w for `warmup` untimed and `steps` timed steps with
+    device-resident inputs (CUDA events on the library's stream, max over
+    ranks), then `phase_steps` profiled steps for the per-phase split."""
+    import torch
+    w = WORKLOADS[name]
+    tr = t.Trainer.from_config(make_config(w, args.family, args.grad,
+                                           not args.no_morton,
+                                           args.morton_bits),
+                               n_input=w["d"], n_output=w["O"], device=local)
+    if world > 1:
+        import torch.distributed as dist
+        uid = [t.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tr.dp_init(uid[0], rank, world)
+    plan = tr.plan()
+    B = w["batch"]
+    # device-resident pool of distinct batches (inputs + working set > L2)
+    pool = []
+    for i in range(4):
+        p, g = make_batch_np(w, B, 1000 * rank + i)
+        pool.append((torch.from_numpy(p).cuda(), torch.from_numpy(g).cuda()))
+    stream = torch.cuda.ExternalStream(tr.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ck = ClockSampler(local) if clocks else None
+    if ck:
+        ck.start()  # sampling covers warm-up (clocks ramp) and timed steps
+    for i in range(warmup):
+        tr.training_step(*pool[i % 4])
+    barrier(world)
+    torch.cuda.synchronize()
+    l0 = tr.launch_count()
+    losses = []
+    ev0.record(stream)
+    for i in range(steps):
+        losses.append(tr.training_step(*pool[i % 4]))
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = tr.launch_count() - l0
+    # per-phase device times from a separate profiled pass (its event
+    # records are not part of the timed steps above)
+    fb, ad, ar, so = [], [], [], []
+    for i in range(phase_steps):
+        tr.training_step(*pool[i % 4], profile=True)
+        r = tr.last_result
+        fb.append(r.fwd_bwd_ms)
+        ad.append(r.adam_ms)
+        ar.append(r.allreduce_ms)
+        so.append(r.sort_ms)
+    clk = ck.stop() if ck else None
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    hbm, peak_note = hbm_peak()
+    nc = 1 << w["d"]
+    tbytes = 2 if w["table"] == "F16" else 4
+    # algorithmic bytes per sample of the forward/backward: every corner's
+    # table entry gathered once and its gradient reduced once, plus the
+    # point's position and target
+    per_sample = w["L"] * nc * w["F"] * (tbytes + 4) + (w["d"] + w["O"]) * 4
+    fb_ms = statistics.mean(fb)
+    achieved = per_sample * B / (fb_ms / 1000.0) / 1e9
+    traffic = NCU_TRAFFIC_PER_SAMPLE.get((name, plan["family"]))
+    l2 = NCU_L2.get((name, plan["family"]))
+    return {
+        "trainer": tr, "plan": plan, "pool": pool, "stream": stream,
+        "family": plan["family"],
+        "value": world * steps / (ms / 1000.0), "ms_per_step": ms / steps,
+        "launches": launches, "final_loss": losses[-1] if losses else None,
+        "clocks": clk, "n_params": tr.hash_count + tr.mlp_count,
+        "phase_ms": {"sort": statistics.mean(so), "fwd_bwd": fb_ms,
+                     "allreduce": statistics.mean(ar),
+                     "adam": statistics.mean(ad)},
+        "roofline": {"kernel": "fwd_bwd (" + plan["family"] + ")",
+                     "bound": "hbm", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": peak_note,
+                     "algorithmic_bytes_per_sample": per_sample,
+                     "traffic": None if traffic is None else traffic * B,
+                     "traffic_unit": "bytes per launch (ncu dram read+write)"},
+        "roofline_l2": None if l2 is None else {
+            "kernel": "fwd_bwd (" + plan["family"] + ")", "bound": "l2",
+            "achieved": l2[0] * B / (fb_ms / 1000.0) / 1e9, "unit": "GB/s",
+            "frac": l2[1] / 100.0,
+            "source": "lts__t_bytes per sample of one ncu capture over this "
+                      "run's kernel time; frac = that capture's "
+                      "lts__throughput (pct of peak sustained)"},
+    }
+
+
+def adam_traffic_bytes(tr, batch, w):
+    """Algorithmic bytes of one sparse Adam launch for a batch like `batch`:
+    the kernel reads every hash gradient (4 B) and the touched map, and for
+    each group of four parameters holding a touched slot reads and writes w,
+    m, v (24 B each), clears the gradient (4 B) and, with an fp16 table,
+    writes the gather copy (2 B); the MLP is updated densely (28 B each)."""
+    tr.zero_gradients()
+    tr.forward_backward(*batch)
+    touched = tr.read_buffer(21)
+    tr.zero_gradients()
+    hc = tr.hash_count
+    width = 2 if w["F"] == 2 else 1
+    per_q = 4 // width                      # tracked slots per group of four
+    groups = touched[: (touched.size // per_q) * per_q].reshape(-1, per_q).any(1)
+    active = int(groups.sum())
+    tb = 2 if w["table"] == "F16" else 0
+    nbytes = hc * 4 + touched.size + active * 4 * (24 + 4 + tb) + tr.mlp_count * 28
+    return {"bytes": nbytes, "active_fraction": active / max(groups.size, 1)}
+
+
+def dp_parity_check(t, tr, rank, world, local):
+    """Data-parallel correctness on the hardware that was just timed, outside
+    the timed region (every rank calls it; rank 0 gets the result):
+
+    1. the benchmark trainer's state after the timed steps: every rank's fp32
+       table and MLP (gathered with dp_sync_state when the optimizer is
+       sharded) hash to the same digest;
+    2. a replay with the benchmark's formats (FullyFused, fp16 gather copy,
+       float gradients, Morton sort) on a small table: 3 data-parallel steps
+       of 4096 points per rank, then rank 0 alone trains a fresh trainer on
+       the concatenated batches; losses within 1e-3, weight changes aligned
+       (cosine >= 0.999), and the slots that moved are the same;
+    3. the same with int32 fixed-point gradients for one step: the summed
+       hash gradient is exact in any order, so the hash table after the step
+       is bit-identical to the single-process one.
+
+    This covers the 2-rank allreduce and, from 4 ranks, the reduce-scatter /
+    shard Adam / all-gather update."""
+    import hashlib
+    import torch.distributed as dist
+    res = {}
+    tr.dp_sync_state()
+    hw, mw = tr.weights()
+    dg = hashlib.blake2b(hw.tobytes() + mw.tobytes(), digest_size=16).hexdigest()
+    digests = [None] * world
+    dist.all_gather_object(digests, dg)
+    res["replicas_identical"] = len(set(digests)) == 1
+
+    def small(grad):
+        w = dict(L=8, F=2, log2T=14, d=3, base=16.0, scale=1.447, W=64, H=1,
+                 O=1, loss="L1", lr=1e-2, table="F16")
+        return t.Trainer.from_config(make_config(w, "FullyFused", grad, True),
+                                     n_input=3, n_output=1, device=local)
+
+    def batches(steps, n):
+        rng = np.random.default_rng(4321)
+        c, r = sphere_params()
+        out = []
+        for _ in range(steps):
+            pos = rng.uniform(-1, 1, (n, 3)).astype(np.float32)
+            d = np.linalg.norm(pos[:, None, :] - c[None], axis=2) - r[None]
+            out.append((pos, d.min(axis=1, keepdims=True).astype(np.float32)))
+        return out
+
+    def dp_run(grad, steps, n):
+        a = small(grad)
+        uid = [t.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        a.dp_init(uid[0], rank, world)
+        h0, m0 = a.weights()
+        losses = []
+        for pos, tgt in batches(steps, n * world):
+            sl = slice(rank * n, (rank + 1) * n)
+            losses.append(a.training_step(np.ascontiguousarray(pos[sl]),
+                                          np.ascontiguousarray(tgt[sl])))
+        a.dp_sync_state()
+        h, m = a.weights()
+        a.close()
+        return h0, m0, h, m, losses
+
+    def single(grad, steps, n):
+        b = small(grad)
+        losses = [b.training_step(p, g) for p, g in batches(steps, n * world)]
+        h, m = b.weights()
+        b.close()
+        return h, m, losses
+
+    def cos(a, b):
+        a, b = a.astype(np.float64), b.astype(np.float64)
+        return float(a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300))
+
+    n = 4096
+    h0, m0, h, m, la = dp_run("F32", 3, n)
+    hf0, mf0, hf, mf, _ = dp_run("Fixed16", 1, n)
+    if rank == 0:
+        hs, ms, lb = single("F32", 3, n)
+        res["f32_3_steps"] = {
+            "loss_max_rel": float(max(abs(x - y) / max(abs(y), 1e-30)
+                                      for x, y in zip(la, lb))),
+            "hash_delta_cosine": cos(h - h0, hs - h0),
+            "mlp_delta_cosine": cos(m - m0, ms - m0),
+            "moved_slots_mismatch": float(np.mean(
+                (h != h0).reshape(-1, 2).any(1) != (hs != h0).reshape(-1, 2).any(1))),
+        }
+        hsf, msf, _ = single("Fixed16", 1, n)
+        res["fixed16_1_step"] = {
+            "hash_bit_identical": bool(np.array_equal(hf.view(np.uint32),
+                                                      hsf.view(np.uint32))),
+            "mlp_max_abs_diff": float(np.abs(mf - msf).max()),
+        }
+        f = res["f32_3_steps"]
+        ok = (res["replicas_identical"] and f["loss_max_rel"] <= 1e-3 and
+              f["hash_delta_cosine"] >= 0.999 and f["mlp_delta_cosine"] >= 0.999
+              and f["moved_slots_mismatch"] <= 1e-3 and
+              res["fixed16_1_step"]["hash_bit_identical"])
+        res["status"] = "ok" if ok else "FAIL"
+        res["path"] = "sharded optimizer (reduce-scatter, shard Adam, all-gather)" \
+            if world >= 4 else "replicated optimizer (allreduce)"
+    dist.barrier()
+    return res
 
 
 def cpu_baseline(w, seconds=12.0):
@@ -566,6 +791,8 @@ def main():
                     help="Morton sort key bits (0: the whole code)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-subworkloads", action="store_true",
+                    help="skip the image / field4d sub-results")
     ap.add_argument("--only", default=None,
                     help="mlp_sweep: one point W:H:log2N (e.g. 64:4:20)")
     args = ap.parse_args()
@@ -601,55 +828,12 @@ def main():
     import torch
     import tmnn_b200 as t
     torch.cuda.set_device(local)
-    tr = t.Trainer.from_config(make_config(w, args.family, args.grad,
-                                           not args.no_morton,
-                                           args.morton_bits),
-                               n_input=w["d"], n_output=w["O"], device=local)
-    if world > 1:
-        import torch.distributed as dist
-        uid = [t.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        # NCCL prints its version on stdout at communicator creation; keep
-        # stdout for the single JSON line
-        tr.dp_init(uid[0], rank, world)
-    plan = tr.plan()
-    B = w["batch"]
-    # device-resident pool of distinct batches (inputs + working set > L2)
-    pool = []
-    for i in range(4):
-        p, g = make_batch_np(w, B, 1000 * rank + i)
-        pool.append((torch.from_numpy(p).cuda(), torch.from_numpy(g).cuda()))
-    stream = torch.cuda.ExternalStream(tr.stream())
+    run = time_training(t, args.workload, args, rank, world, local, args.steps,
+                        args.warmup, phase_steps=min(args.steps, 50),
+                        clocks=True)
+    tr, plan, pool, stream = run["trainer"], run["plan"], run["pool"], run["stream"]
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-
-    clocks = ClockSampler(local)
-    clocks.start()  # sampling covers warm-up (clocks ramp) and timed steps
-    for i in range(args.warmup):
-        tr.training_step(*pool[i % 4])
-    barrier(world)
-    torch.cuda.synchronize()
-    l0 = tr.launch_count()
-    losses = []
-    ev0.record(stream)
-    for i in range(args.steps):
-        losses.append(tr.training_step(*pool[i % 4]))
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    launches = tr.launch_count() - l0
-    # per-phase device times from a separate profiled pass (its event
-    # records are not part of the timed steps above)
-    fb, ad, ar, so = [], [], [], []
-    for i in range(min(args.steps, 50)):
-        tr.training_step(*pool[i % 4], profile=True)
-        r = tr.last_result
-        fb.append(r.fwd_bwd_ms)
-        ad.append(r.adam_ms)
-        ar.append(r.allreduce_ms)
-        so.append(r.sort_ms)
-    ck = clocks.stop()
-    barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1), world)
-    value = world * args.steps * B / (ms / 1000.0) / B
+    B = w["batch"]
     unit = "steps/s (2^18-point batches)"
 
     # inference samples/s (2^20 points per call, device resident)
@@ -716,30 +900,41 @@ def main():
                "h2d_bytes_per_step": int(hpool[0][0].nbytes + hpool[0][1].nbytes),
                "d2h_bytes_per_step": 8}
 
+    adam_bytes = adam_traffic_bytes(tr, pool[0], w)
+    dp_parity = dp_parity_check(t, tr, rank, world, local) if world > 1 else None
+    tr.close()
+
+    # the north-star workloads beside the headline one, same protocol,
+    # fewer steps (image: the >= 1000 steps/s target; field4d: BASELINE
+    # configs[4], the 8-GPU scaling target)
+    subs = {}
+    if not args.no_subworkloads and w.get("kind") is None:
+        for name in ("image", "field4d"):
+            if name == args.workload:
+                continue
+            r = time_training(t, name, args, rank, world, local,
+                              steps=min(args.steps, 40), warmup=5,
+                              phase_steps=10)
+            r["trainer"].close()
+            subs[name] = {k: r[k] for k in ("value", "ms_per_step", "phase_ms",
+                                            "family", "final_loss",
+                                            "roofline")}
+            subs[name]["unit"] = unit
+            subs[name]["desc"] = WORKLOADS[name]["desc"]
+            subs[name]["samples_per_s"] = r["value"] * WORKLOADS[name]["batch"]
+            del r
+            torch.cuda.empty_cache()
+
     if rank != 0:
-        tr.close()
         return
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except (OSError, ValueError):
-        pass
-    hbm = peaks.get("hbm_gbs")
-    peak_note = "measured" if hbm else "fallback"
-    hbm = hbm or 6650.0
-    nc = 1 << w["d"]
-    tbytes = 2 if w["table"] == "F16" else 4
-    per_sample = w["L"] * nc * w["F"] * (tbytes + 4) + (w["d"] + w["O"]) * 4
-    fb_ms = statistics.mean(fb)
-    achieved = per_sample * B / (fb_ms / 1000.0) / 1e9
-    traffic = NCU_TRAFFIC_PER_SAMPLE.get((args.workload, plan["family"]))
-    n_params = tr.hash_count + tr.mlp_count
-    adam_bytes = n_params * (4 * 7 + (2 if w["table"] == "F16" else 0)) + \
-        (n_params // 2)  # w,m,v r/w + grad r/w + touched
+    hbm, peak_note = hbm_peak()
+    n_params = run["n_params"]
+    ad_ms = run["phase_ms"]["adam"]
     line = {
         "metric": "training steps/s (HashGrid+FusedMLP, 2^18-point batches)",
-        "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "value": run["value"], "unit": unit, "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": run["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 table / f32 accumulate" if w["table"] == "F16" else "f32",
         "data": "synthetic",
@@ -751,33 +946,37 @@ def main():
                    "morton_key_bits": args.morton_bits,
                    "l2": "no flush: per-step working set (fp32 params, m, v, "
                          "grads, fp16 gather copy) exceeds the 126 MB L2"},
-        "samples_per_s": value * B,
+        "samples_per_s": run["value"] * B,
         "inference_samples_per_s": inf_sps,
         "eval_gradient": eg,
-        "final_loss": losses[-1],
-        "phase_ms": {"sort": statistics.mean(so), "fwd_bwd": fb_ms,
-                     "allreduce": statistics.mean(ar),
-                     "adam": statistics.mean(ad)},
-        "roofline": {"kernel": "fwd_bwd (" + plan["family"] + ")",
-                     "bound": "hbm", "achieved": achieved, "peak": hbm,
-                     "unit": "GB/s", "frac": achieved / hbm,
-                     "peak_source": peak_note,
-                     "algorithmic_bytes_per_sample": per_sample,
-                     "traffic": None if traffic is None else traffic * B,
-                     "traffic_unit": "bytes per launch (ncu)"},
-        "roofline_adam": {"bound": "hbm",
-                          "achieved": adam_bytes / (statistics.mean(ad) / 1e3) / 1e9,
+        "final_loss": run["final_loss"],
+        "phase_ms": run["phase_ms"],
+        "roofline": run["roofline"],
+        "roofline_l2": run["roofline_l2"],
+        "roofline_adam": {"kernel": "k_adam_hash4 (+ MLP)", "bound": "hbm",
+                          "achieved": adam_bytes["bytes"] / (ad_ms / 1e3) / 1e9,
                           "peak": hbm, "unit": "GB/s",
-                          "frac": adam_bytes / (statistics.mean(ad) / 1e3) / 1e9 / hbm},
-        "gpu_launches": int(launches),
-        "clocks": ck,
+                          "frac": adam_bytes["bytes"] / (ad_ms / 1e3) / 1e9 / hbm,
+                          "peak_source": peak_note,
+                          "algorithmic_bytes": adam_bytes["bytes"],
+                          "active_fraction": adam_bytes["active_fraction"],
+                          "note": "bytes counted over the groups of four "
+                                  "parameters the kernel updates (touched), "
+                                  "plus the gradient read of every element; "
+                                  "the adam phase also holds the one-block "
+                                  "numerics probe"},
+        "gpu_launches": int(run["launches"]),
+        "clocks": run["clocks"],
         "e2e": e2e,
+        "n_params": n_params,
     }
+    if subs:
+        line["subworkloads"] = subs
+    if dp_parity is not None:
+        line["dp_parity"] = dp_parity
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(w)
-    tr.close()
     emit(line)
-
 
 if __name__ == "__main__":
     main()

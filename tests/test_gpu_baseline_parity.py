@@ -150,7 +150,7 @@ def test_adam_step_at_baseline_size_is_bit_exact(name):
     tr.zero_gradients()
     pos, tgt = make_batch(name, N, seed=13)
     tr.forward_backward(pos, tgt)
-    step = tr.step
+    step = tr.step()
     w0 = np.concatenate(tr.weights())
     m0, v0 = tr.read_buffer(8), tr.read_buffer(9)
     gh, gm, touched = tr.read_buffer(3), tr.read_buffer(4), tr.read_buffer(21)
