@@ -24,6 +24,7 @@
 #include "../../include/tmnn_cuda.h"
 #include "fused.h"
 #include "kernels.h"
+#include "tiled.h"
 #include "runtime.h"
 
 using namespace tmnn;
@@ -154,6 +155,8 @@ struct tmnn_ctx {
   DevBuf<float> grad_out, eg_scratch;  // evaluate_with_gradient
   DevBuf<uint32_t> codes, codes_alt, idx, perm;
   DevBuf<uint8_t> sort_tmp;
+  DevBuf<__half> feat;   // Tiled family: encoded features [N x In]
+  DevBuf<float> dfeat;   // Tiled family: dL/d(features) [N x In]
   StepStats *h_stats = nullptr;  // pinned copy of the step statistics
   double *h_loss = nullptr;      // &h_stats->loss
   // numerics guard
@@ -174,6 +177,13 @@ struct tmnn_ctx {
   float *hash_w() { return params.p; }
   float *mlp_w() { return params.p + hash_count; }
   const float *gather_table() const { return params.p; }
+  // the fp16 gather copy the tensor-core families read (null: fp32 table)
+  const __half *gather_half() const {
+    return spec.table_dtype == TMNN_DTYPE_F16 ? table_h.p : nullptr;
+  }
+  bool tensor_core_family() const {
+    return family == TMNN_FAMILY_FULLY_FUSED || family == TMNN_FAMILY_TILED;
+  }
 
   ~tmnn_ctx() {
     if (stream) cudaStreamSynchronize(stream);
@@ -363,34 +373,64 @@ NetDims make_dims(const tmnn_spec &s, const tmnn_train_cfg &c) {
   return nd;
 }
 
+// NetworkPlanner::plan_with_capabilities (network_planner.cpp:132-290):
+// forced families win; Auto takes FullyFused when its kernel supports the
+// shape, except that when the table's gather copy plus its fp32 gradients
+// exceed the L2 the level-major Tiled family is selected (the fused
+// kernel's point-major gathers and reductions would go to HBM).  When the
+// tensor-core kernels cannot run the shape at all, SafeDebug (fp32 CUDA
+// cores) runs it, with the reason recorded and a warning on stderr.
 void plan_family(tmnn_ctx &c) {
-  std::string why;
+  std::string why, why_t;
   const bool fused_ok = fused_supported(c.spec, c.cfg, &why);
+  const bool tiled_ok = tiled_supported(c.nd, &why_t);
   const int want = c.cfg.family;
+  int l2 = 0;
+  cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, c.device);
+  const uint64_t tbytes = c.spec.table_dtype == TMNN_DTYPE_F16 ? 2 : 4;
+  const uint64_t resident = c.nd.hash_count * (tbytes + 4);
+  const bool overflows_l2 = l2 > 0 && resident > (uint64_t)l2;
+  auto fallback_reason = [](const std::string &w) {
+    return w.find("hidden") != std::string::npos   ? kReasonHiddenDimUnsupported
+           : w.find("output") != std::string::npos ? kReasonUnsupportedOutputDims
+                                                   : kReasonUnsupportedInputDims;
+  };
   if (want == TMNN_FAMILY_SAFE_DEBUG) {
     c.family = TMNN_FAMILY_SAFE_DEBUG;
     c.fallback_reason = kReasonForcedSafeDebug;
     c.plan_text = "SafeDebug requested";
   } else if (want == TMNN_FAMILY_TILED) {
-    // The tiled family (separate encode / MLP / scatter launches) runs the
-    // same fp32 reference-order kernels as SafeDebug on this build.
+    if (!tiled_ok)
+      throw std::invalid_argument("Tiled family unavailable: " + why_t);
     c.family = TMNN_FAMILY_TILED;
     c.fallback_reason = kReasonForcedTiled;
-    c.plan_text = "Tiled requested";
+    c.plan_text = "Tiled requested: level-major encode, tcgen05 MLP, "
+                  "level-major scatter";
+  } else if (want == TMNN_FAMILY_FULLY_FUSED) {
+    if (!fused_ok)
+      throw std::invalid_argument("FullyFused family unavailable: " + why);
+    c.family = TMNN_FAMILY_FULLY_FUSED;
+    c.fallback_reason = kReasonNone;
+    c.plan_text = "FullyFused requested: tcgen05 fused step";
+  } else if (fused_ok && tiled_ok && overflows_l2) {
+    c.family = TMNN_FAMILY_TILED;
+    c.fallback_reason = kReasonNone;
+    c.plan_text = "Tiled: gather table + gradients (" +
+                  std::to_string(resident >> 20) + " MiB) exceed the L2 (" +
+                  std::to_string((uint64_t)l2 >> 20) +
+                  " MiB): level-major encode and scatter";
   } else if (fused_ok) {
     c.family = TMNN_FAMILY_FULLY_FUSED;
     c.fallback_reason = kReasonNone;
     c.plan_text = "FullyFused: tcgen05 fused step";
-  } else if (want == TMNN_FAMILY_FULLY_FUSED) {
-    throw std::invalid_argument("FullyFused family unavailable: " + why);
   } else {
     c.family = TMNN_FAMILY_SAFE_DEBUG;
-    c.fallback_reason = why.find("hidden") != std::string::npos
-                            ? kReasonHiddenDimUnsupported
-                        : why.find("output") != std::string::npos
-                            ? kReasonUnsupportedOutputDims
-                            : kReasonEncodingRequiresTiledFamily;
-    c.plan_text = "SafeDebug fallback: " + why;
+    c.fallback_reason = fallback_reason(why);
+    c.plan_text = "SafeDebug fallback (fp32 CUDA cores, no tensor cores): " + why;
+    std::fprintf(stderr,
+                 "tmnn: warning: this network shape leaves the tensor-core "
+                 "path (%s); training runs on the fp32 SafeDebug kernels\n",
+                 why.c_str());
   }
 }
 
@@ -497,6 +537,10 @@ void reset_optimizer(tmnn_ctx &c) {
 
 void ensure_batch(tmnn_ctx &c, uint32_t N) {
   const size_t d = c.nd.d, O = c.nd.O;
+  if (c.family == TMNN_FAMILY_TILED) {
+    c.feat.ensure((size_t)N * c.nd.In);
+    c.dfeat.ensure((size_t)N * c.nd.In);
+  }
   c.pos_in.ensure(N * d);
   c.tgt_in.ensure(N * O);
   c.pos_s.ensure(N * d);
@@ -559,6 +603,14 @@ void fwd_bwd(tmnn_ctx &c, const float *pos, const float *tgt,
                               c.num_sms, c.stream, c.implicit_touch);
     return;
   }
+  if (c.family == TMNN_FAMILY_TILED) {
+    c.launches += tiled_train(c.fws, c.nd, c.params.p, c.gather_half(), pos,
+                              tgt, dext, inv_N, c.gm.p, c.gh_fixed.p,
+                              c.gh_float.p, c.touched.p, c.loss_acc.p,
+                              c.feat.p, c.dfeat.p, N, c.num_sms, c.stream,
+                              c.implicit_touch);
+    return;
+  }
   launch_train_exact(c.nd, c.hash_w(), c.mlp_w(), pos, tgt, dext, inv_N,
                      c.gm.p, c.gh_fixed.p, c.gh_float.p, c.touched.p,
                      c.loss_acc.p, N, c.scratch.p, c.num_sms, c.stream);
@@ -570,6 +622,11 @@ void forward_dev(tmnn_ctx &c, const float *pos, float *out, uint32_t N) {
   if (c.family == TMNN_FAMILY_FULLY_FUSED) {
     c.launches += fused_forward(c.fws, c.nd, c.spec, c.params.p, c.table_h.p,
                                 pos, out, N, c.num_sms, c.stream);
+    return;
+  }
+  if (c.family == TMNN_FAMILY_TILED) {
+    c.launches += tiled_forward(c.fws, c.nd, c.params.p, c.gather_half(), pos,
+                                out, c.feat.p, N, c.num_sms, c.stream);
     return;
   }
   launch_forward_exact(c.nd, c.hash_w(), c.mlp_w(), pos, out, N, c.scratch.p,
@@ -717,7 +774,7 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
   if (c.gh_float.p)
     CK(cudaMemsetAsync(c.gh_float.p, 0, c.gh_float.bytes(), c.stream));
   CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
-  if (c.family == TMNN_FAMILY_FULLY_FUSED && c.table_h.p) {
+  if (c.tensor_core_family() && c.table_h.p) {
     // the fused kernels read only the fp16 gather copy of the table: gather
     // that (half the bytes); the fp32 master stays sharded until synced
     NK(ncclAllGather(c.table_h.p + off, c.table_h.p, shard, ncclHalf, c.comm,
@@ -795,7 +852,7 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   c.v.alloc(total);
   if (spec.table_dtype == TMNN_DTYPE_F16) c.table_h.alloc(c.hash_count);
   plan_family(c);
-  c.implicit_touch = c.family == TMNN_FAMILY_FULLY_FUSED && !c.nd.grad_fixed;
+  c.implicit_touch = c.tensor_core_family() && !c.nd.grad_fixed;
   if (c.nd.grad_fixed)
     c.gh_fixed.alloc(c.hash_count);
   else
@@ -1313,7 +1370,13 @@ tmnn_status tmnn_cuda_forward_backward_noalloc(tmnn_ctx *c,
     if (c->nd.O > (int)kNoAllocMaxOutputs)
       throw std::invalid_argument(
           "forward_backward_noalloc: more than 16 outputs are not supported");
-    if (c->family == TMNN_FAMILY_FULLY_FUSED &&
+    if (c->family == TMNN_FAMILY_TILED &&
+        (c->feat.n < (size_t)n * c->nd.In || c->dfeat.n < (size_t)n * c->nd.In))
+      throw std::invalid_argument(
+          "forward_backward_noalloc: the Tiled family's feature buffers are "
+          "smaller than this batch; run one ordinary training_step or "
+          "forward_backward with at least this many points first");
+    if (c->tensor_core_family() &&
         (!c->fws.err || !c->fws.wpack))
       throw std::invalid_argument(
           "forward_backward_noalloc: the fused kernel's weight image is not set "

@@ -18,6 +18,7 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
 enum PlannerFallbackReason : int32_t {
   kReasonNone = 0,
   kReasonNoGPUContext = 1,
+  kReasonUnsupportedInputDims = 6,
   kReasonUnsupportedOutputDims = 7,
   kReasonHiddenDimUnsupported = 9,
   kReasonForcedTiled = 10,
