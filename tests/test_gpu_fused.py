@@ -21,6 +21,13 @@ CASES = [
     dict(L=4, F=4, log2T=12, d=3, W=64, H=3, O=2, loss=0),
     dict(L=8, F=2, log2T=12, d=3, W=128, H=1, O=16, loss=0),
     dict(L=8, F=2, log2T=12, d=3, W=64, H=4, O=3, loss=3),
+    # narrow and deep networks (tensor-core training for W = 16 / 32 pads the
+    # weight-gradient MMAs to M = 64; up to 8 hidden layers)
+    dict(L=16, F=2, log2T=12, d=3, W=16, H=1, O=1, loss=1),
+    dict(L=8, F=2, log2T=12, d=3, W=32, H=2, O=3, loss=0),
+    dict(L=8, F=2, log2T=12, d=3, W=32, H=8, O=1, loss=0),
+    dict(L=8, F=2, log2T=12, d=4, W=16, H=6, O=4, loss=0, base=8.0, scale=1.5),
+    dict(L=8, F=2, log2T=12, d=3, W=64, H=5, O=2, loss=2, huber=0.1),
 ]
 
 

@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kTile = 128;
 constexpr int kThreads = 256;
-constexpr int kMaxTrainHidden = 4;
+constexpr int kMaxTrainHidden = 8;
 constexpr int kOutCols = 16;  // output layer padded to N = 16
 // Levels whose resolution is at most this are scattered with warp
 // aggregation (coarse grids: many points of a Morton-sorted warp share
@@ -104,7 +104,10 @@ Layout make_layout(const NetDims &nd, bool train, bool stream = false) {
     off = L.tail_dst + L.tail_bytes;
   }
   L.xc = train ? In + 16 : In;
-  L.hc = train ? W + 16 : W;
+  // training tiles: W activation columns, a ones column block (bias
+  // gradients), and at least 64 columns in all, since the weight-gradient
+  // MMAs read dH^T as an M = 64 operand when W < 64
+  L.hc = train ? (W + 16 > 64 ? W + 16 : 64) : W;
   L.x = off;
   off = align128(off + kTile * L.xc * 2);
   L.n_h_tiles = train ? H : (H > 1 ? 2 : 1);
@@ -321,6 +324,9 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
   const int half = t >> 7;         // which part of the work on that row
   const int In = nd.In, H = nd.H, O = nd.O;
   constexpr int LPC = 8 / F;       // levels per 8-column chunk
+  // rows of the weight-gradient MMAs (M = W, padded to the smallest M of
+  // a one-CTA tcgen05.mma, 64; the padding rows are never flushed)
+  constexpr int MW = W < 64 ? 64 : W;
   constexpr int NL = D == 4 ? 1 : (LPC < 2 ? LPC : 2);  // levels per load batch
   const int n_chunks = In / 8;
   uint64_t *mbar = reinterpret_cast<uint64_t *>(sm + Ly.misc);
@@ -336,8 +342,12 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
     if (TRAIN && half == 0) {
       float ones[16] = {1.f};
       store_row16(X, Ly.xc, r, In, ones);
-      for (int k = 0; k < H; ++k)
+      const float zeros[16] = {0.f};
+      for (int k = 0; k < H; ++k) {
         store_row16(reinterpret_cast<__half *>(sm + Ly.h[k]), Ly.hc, r, W, ones);
+        for (int c0 = W + 16; c0 < Ly.hc; c0 += 16)  // M = 64 padding (W < 64)
+          store_row16(reinterpret_cast<__half *>(sm + Ly.h[k]), Ly.hc, r, c0, zeros);
+      }
     }
     if (t < 20) s_red[t] = 0.f;
     if (t == 0) tc::mbar_init(tc::smem_u32(mbar), 1);
@@ -499,7 +509,7 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
                tc::Operand{sbase + Ly.sw[H], kOutCols, 0}, kTile, W, kOutCols, 0);
       // dWout += H^T . dY
       tc::gemm(tmem + Ly.t_dwout, tc::Operand{sbase + Ly.h[hl], Ly.hc, 1},
-               tc::Operand{sbase + Ly.dy, kOutCols, 1}, W, kOutCols, kTile,
+               tc::Operand{sbase + Ly.dy, kOutCols, 1}, MW, kOutCols, kTile,
                first ? 0u : 1u);
       tc::commit(mbar_a);
     }
@@ -528,11 +538,11 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
         if (k > 0) {
           tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.sw[k], W, 0}, kTile, W, W, 0);
           tc::gemm(tmem + Ly.t_dwk[k], dHkT,
-                   tc::Operand{sbase + Ly.h[k - 1], Ly.hc, 1}, W, W + 16, kTile,
+                   tc::Operand{sbase + Ly.h[k - 1], Ly.hc, 1}, MW, W + 16, kTile,
                    first ? 0u : 1u);
         } else {
           tc::gemm(T_s, dHk, tc::Operand{sbase + Ly.sw[0], W, 0}, kTile, In, W, 0);
-          tc::gemm(tmem + Ly.t_dw0, dHkT, tc::Operand{sbase + Ly.x, Ly.xc, 1}, W,
+          tc::gemm(tmem + Ly.t_dw0, dHkT, tc::Operand{sbase + Ly.x, Ly.xc, 1}, MW,
                    In + 16, kTile, first ? 0u : 1u);
         }
         tc::commit(mbar_a);
@@ -652,8 +662,8 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
     // M = W: row rr of an accumulator lives in lane rr (W == 128) or in lane
     // (rr / 16) * 32 + rr % 16 (W == 64).
     const int lane = t & 31;
-    const bool has_row = W == 128 || lane < 16;
     const int rr = W == 128 ? r : (warp & 3) * 16 + lane;
+    const bool has_row = (W == 128 || lane < 16) && rr < W;
     const float s = P.inv_dscale;
     auto flush = [&](uint32_t tcol, int ncols, auto &&dest) {
       for (int c0 = half * 16; c0 < ncols; c0 += 16 * Q) {
@@ -1064,8 +1074,8 @@ using KernelFn = void (*)(FusedParams);
 template <int D, int F, bool HALF, bool TRAIN>
 KernelFn pick_w(int W) {
   switch (W) {
-    case 16: return TRAIN ? nullptr : (KernelFn)k_fused<D, F, 16, HALF, TRAIN>;
-    case 32: return TRAIN ? nullptr : (KernelFn)k_fused<D, F, 32, HALF, TRAIN>;
+    case 16: return (KernelFn)k_fused<D, F, 16, HALF, TRAIN>;
+    case 32: return (KernelFn)k_fused<D, F, 32, HALF, TRAIN>;
     case 64: return (KernelFn)k_fused<D, F, 64, HALF, TRAIN>;
     case 128: return (KernelFn)k_fused<D, F, 128, HALF, TRAIN>;
   }
@@ -1105,8 +1115,9 @@ bool shape_ok(const NetDims &nd, bool train, std::string *why) {
     return no("encoding width (levels x features) must be a multiple of 16, <= 128");
   if (nd.O > kOutCols) return no("more than 16 outputs");
   if (train) {
-    if (nd.W != 64 && nd.W != 128) return no("hidden width must be 64 or 128");
-    if (nd.H > kMaxTrainHidden) return no("more than 4 hidden layers");
+    if (nd.W != 16 && nd.W != 32 && nd.W != 64 && nd.W != 128)
+      return no("hidden width must be 16, 32, 64 or 128");
+    if (nd.H > kMaxTrainHidden) return no("more than 8 hidden layers");
   } else if (nd.W != 16 && nd.W != 32 && nd.W != 64 && nd.W != 128) {
     return no("hidden width must be 16, 32, 64 or 128");
   }

@@ -168,11 +168,18 @@ struct tmnn_ctx {
   FusedWorkspace fws;
   // data parallelism
   ncclComm_t comm = nullptr;
+  // bucketed exchange (Tiled family): the gradient collectives run on
+  // comm_stream, one bucket of levels at a time, behind the scatter
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t dp_ev[kMaxLevels + 2] = {};
+  int dp_buckets = 4;
   int rank = 0, world = 1;
   // sharded data-parallel optimizer: this rank's copies of the fp32 table
   // outside its shard, and of m and v outside its shard, are out of date
   // until tmnn_cuda_dp_sync_state gathers them
   bool stale = false;
+  // level ranges [l0, l1) whose per-rank shards the stale state follows
+  std::vector<std::pair<int, int>> stale_layout;
 
   float *hash_w() { return params.p; }
   float *mlp_w() { return params.p + hash_count; }
@@ -188,6 +195,12 @@ struct tmnn_ctx {
   ~tmnn_ctx() {
     if (stream) cudaStreamSynchronize(stream);
     if (comm) ncclCommDestroy(comm);
+    if (comm_stream) {
+      cudaStreamSynchronize(comm_stream);
+      cudaStreamDestroy(comm_stream);
+    }
+    for (auto e : dp_ev)
+      if (e) cudaEventDestroy(e);
     if (h_stats) cudaFreeHost(h_stats);
     for (auto e : ev)
       if (e) cudaEventDestroy(e);
@@ -715,20 +728,208 @@ bool can_shard(const tmnn_ctx &c) {
          c.slots % (uint64_t)c.world == 0;
 }
 
+// ---- bucketed data-parallel exchange (Tiled family) ----------------------
+//
+// The Tiled family scatters the hash gradients level by level, so a group
+// of levels is final while later levels are still being scattered.  The
+// step then runs its collectives on a second stream, bucket by bucket: the
+// MLP gradients and the loss as soon as the MLP kernel is done, each
+// bucket's reduce-scatter (sharded optimizer) or allreduce right after that
+// bucket's scatter launch.  The exchange overlaps the scatter of the later
+// buckets instead of following the whole backward pass.
+struct Bucket {
+  int l0, l1;      // levels
+  uint64_t e0, n;  // table elements of the levels
+};
+
+std::vector<Bucket> dp_bucket_list(const tmnn_ctx &c) {
+  const int L = c.nd.L;
+  int G = c.dp_buckets < 1 ? 1 : (c.dp_buckets > L ? L : c.dp_buckets);
+  std::vector<Bucket> b;
+  const uint64_t per = (uint64_t)c.nd.T * c.nd.F;
+  for (int g = 0; g < G; ++g) {
+    const int l0 = g * L / G, l1 = (g + 1) * L / G;
+    if (l1 > l0) b.push_back({l0, l1, per * l0, per * (uint64_t)(l1 - l0)});
+  }
+  return b;
+}
+
+bool can_overlap(const tmnn_ctx &c) {
+  return c.comm && c.world > 1 && c.comm_stream &&
+         c.family == TMNN_FAMILY_TILED && c.dp_buckets > 1;
+}
+
+// Every bucket splits evenly into groups of four elements per rank (the
+// sharded Adam works on groups of four) and into whole tracked slots.
+bool buckets_shardable(const tmnn_ctx &c, const std::vector<Bucket> &bs) {
+  if (!can_shard(c)) return false;
+  for (const Bucket &b : bs)
+    if (b.n % (4ull * (uint64_t)c.world) != 0 ||
+        (b.n / c.entry_width) % (uint64_t)c.world != 0 ||
+        b.e0 % (uint64_t)c.entry_width != 0)
+      return false;
+  return true;
+}
+
+void fwd_bwd_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
+                        uint32_t N, float inv_N, bool shard, bool with_loss,
+                        const std::vector<Bucket> &bs) {
+  const NetDims &nd = c.nd;
+  const bool fixed = nd.grad_fixed != 0;
+  const bool exch_touched = c.sparse && !c.implicit_touch;
+  c.launches += tiled_encode(nd, c.params.p, c.gather_half(), pos, c.feat.p, N,
+                             c.stream);
+  c.launches += fused_mlp_train(c.fws, nd, c.mlp_w(), c.feat.p, tgt, nullptr,
+                                inv_N, c.gm.p, c.loss_acc.p, c.dfeat.p, N,
+                                c.num_sms, c.stream, 0);
+  CK(cudaEventRecord(c.dp_ev[0], c.stream));
+  CK(cudaStreamWaitEvent(c.comm_stream, c.dp_ev[0], 0));
+  NK(ncclGroupStart());
+  NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
+                   c.comm_stream));
+  if (with_loss)
+    NK(ncclAllReduce(c.loss_acc.p, c.loss_acc.p, 1, ncclFloat64, ncclSum,
+                     c.comm, c.comm_stream));
+  NK(ncclGroupEnd());
+  for (size_t g = 0; g < bs.size(); ++g) {
+    const Bucket &b = bs[g];
+    c.launches += tiled_scatter(nd, pos, c.dfeat.p, c.gh_fixed.p, c.gh_float.p,
+                                c.touched.p, N, c.implicit_touch, c.stream,
+                                b.l0, b.l1);
+    CK(cudaEventRecord(c.dp_ev[1 + g], c.stream));
+    CK(cudaStreamWaitEvent(c.comm_stream, c.dp_ev[1 + g], 0));
+    const uint64_t w = (uint64_t)c.entry_width;
+    NK(ncclGroupStart());
+    if (shard) {
+      const uint64_t gs = b.n / c.world, own = b.e0 + gs * c.rank;
+      if (fixed)
+        NK(ncclReduceScatter(c.gh_fixed.p + b.e0, c.gh_fixed.p + own, gs,
+                             ncclInt32, ncclSum, c.comm, c.comm_stream));
+      else
+        NK(ncclReduceScatter(c.gh_float.p + b.e0, c.gh_float.p + own, gs,
+                             ncclFloat32, ncclSum, c.comm, c.comm_stream));
+      if (exch_touched)
+        NK(ncclReduceScatter(c.touched.p + b.e0 / w, c.touched.p + own / w,
+                             gs / w, ncclUint8, ncclMax, c.comm,
+                             c.comm_stream));
+    } else {
+      if (fixed)
+        NK(ncclAllReduce(c.gh_fixed.p + b.e0, c.gh_fixed.p + b.e0, b.n,
+                         ncclInt32, ncclSum, c.comm, c.comm_stream));
+      else
+        NK(ncclAllReduce(c.gh_float.p + b.e0, c.gh_float.p + b.e0, b.n,
+                         ncclFloat32, ncclSum, c.comm, c.comm_stream));
+      if (exch_touched)
+        NK(ncclAllReduce(c.touched.p + b.e0 / w, c.touched.p + b.e0 / w,
+                         b.n / w, ncclUint8, ncclMax, c.comm, c.comm_stream));
+    }
+    NK(ncclGroupEnd());
+  }
+  CK(cudaEventRecord(c.dp_ev[kMaxLevels + 1], c.comm_stream));
+}
+
+// The main stream waits for the last collective of fwd_bwd_overlapped.
+void join_exchange(tmnn_ctx &c) {
+  CK(cudaStreamWaitEvent(c.stream, c.dp_ev[kMaxLevels + 1], 0));
+}
+
+// Sharded update after a bucketed reduce-scatter: Adam on this rank's
+// shard of every bucket (and on the replicated MLP), reset of the whole
+// local gradient buffer, all-gather of the updated table per bucket (the
+// fp16 gather copy the tensor-core kernels read, else the fp32 table).
+void dp_finish_sharded(tmnn_ctx &c, const std::vector<Bucket> &bs,
+                       const StepStats *guard = nullptr) {
+  AdamArgs a = adam_args(c);
+  a.guard = guard;
+  const uint64_t w = (uint64_t)c.entry_width;
+  for (const Bucket &b : bs) {
+    const uint64_t gs = b.n / c.world, off = b.e0 + gs * c.rank;
+    AdamArgs ah = a;
+    ah.hash_count = gs;
+    ah.slots = gs / w;
+    ah.mlp_count = 0;
+    launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
+                c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
+                c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                c.touched.p + off / w, c.table_h.p ? c.table_h.p + off : nullptr,
+                c.num_sms, c.stream);
+    c.launches++;
+  }
+  launch_adam_mlp(a, c.params.p, c.m.p, c.v.p, c.gm.p, c.num_sms, c.stream);
+  c.launches++;
+  if (c.gh_fixed.p)
+    CK(cudaMemsetAsync(c.gh_fixed.p, 0, c.gh_fixed.bytes(), c.stream));
+  if (c.gh_float.p)
+    CK(cudaMemsetAsync(c.gh_float.p, 0, c.gh_float.bytes(), c.stream));
+  CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
+  const bool half = c.tensor_core_family() && c.table_h.p;
+  NK(ncclGroupStart());
+  for (const Bucket &b : bs) {
+    const uint64_t gs = b.n / c.world, off = b.e0 + gs * c.rank;
+    if (half)
+      NK(ncclAllGather(c.table_h.p + off, c.table_h.p + b.e0, gs, ncclHalf,
+                       c.comm, c.stream));
+    else
+      NK(ncclAllGather(c.params.p + off, c.params.p + b.e0, gs, ncclFloat32,
+                       c.comm, c.stream));
+  }
+  NK(ncclGroupEnd());
+  if (!half && c.table_h.p) {
+    launch_to_half(c.params.p, c.table_h.p, c.hash_count, c.num_sms, c.stream);
+    c.launches++;
+  }
+  c.stale = true;
+  c.stale_layout.clear();
+  for (const Bucket &b : bs) c.stale_layout.push_back({b.l0, b.l1});
+  fused_weights_changed(c.fws);
+  c.step++;
+}
+
+// The shards of the sharded optimizer: per bucket of levels when the Tiled
+// family exchanges bucket by bucket, else one range over the whole table.
+std::vector<Bucket> shard_layout(const tmnn_ctx &c) {
+  if (c.family == TMNN_FAMILY_TILED && c.dp_buckets > 1) {
+    std::vector<Bucket> bs = dp_bucket_list(c);
+    if (bs.size() > 1 && buckets_shardable(c, bs)) return bs;
+  }
+  return {Bucket{0, c.nd.L, 0, c.hash_count}};
+}
+
+bool layout_is(const tmnn_ctx &c, const std::vector<Bucket> &bs) {
+  if (c.stale_layout.size() != bs.size()) return false;
+  for (size_t i = 0; i < bs.size(); ++i)
+    if (c.stale_layout[i].first != bs[i].l0 || c.stale_layout[i].second != bs[i].l1)
+      return false;
+  return true;
+}
+
+void dp_sync_state(tmnn_ctx &c);
+
+// Data-parallel update with the optimizer sharded over the ranks (ZeRO-1
+// style): reduce-scatter the hash gradients and touched map so each rank
+// owns 1/world of every shard range, Adam on those shards only (MLP
+// replicated after an allreduce), then all-gather the updated table.  Same
+// bytes on NVLink as one allreduce, 1/world of the table's Adam work per
+// rank.  With `probe` the numerics probe scans this rank's shards and the
+// ranks combine its results, so every rank takes the same decision.
 void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
                bool probe = false, bool gate = false) {
-  const size_t shard = c.hash_count / c.world, off = shard * c.rank;
-  const size_t sslots = c.slots / c.world, soff = sslots * c.rank;
+  const std::vector<Bucket> bs = shard_layout(c);
+  if (c.stale && !layout_is(c, bs)) dp_sync_state(c);
+  const uint64_t w = (uint64_t)c.entry_width;
   NK(ncclGroupStart());
-  if (c.nd.grad_fixed)
-    NK(ncclReduceScatter(c.gh_fixed.p, c.gh_fixed.p + off, shard, ncclInt32,
-                         ncclSum, c.comm, c.stream));
-  else
-    NK(ncclReduceScatter(c.gh_float.p, c.gh_float.p + off, shard, ncclFloat32,
-                         ncclSum, c.comm, c.stream));
-  if (c.sparse && !c.implicit_touch)
-    NK(ncclReduceScatter(c.touched.p, c.touched.p + soff, sslots, ncclUint8,
-                         ncclMax, c.comm, c.stream));
+  for (const Bucket &b : bs) {
+    const uint64_t gs = b.n / c.world, own = b.e0 + gs * c.rank;
+    if (c.nd.grad_fixed)
+      NK(ncclReduceScatter(c.gh_fixed.p + b.e0, c.gh_fixed.p + own, gs,
+                           ncclInt32, ncclSum, c.comm, c.stream));
+    else
+      NK(ncclReduceScatter(c.gh_float.p + b.e0, c.gh_float.p + own, gs,
+                           ncclFloat32, ncclSum, c.comm, c.stream));
+    if (c.sparse && !c.implicit_touch)
+      NK(ncclReduceScatter(c.touched.p + b.e0 / w, c.touched.p + own / w,
+                           gs / w, ncclUint8, ncclMax, c.comm, c.stream));
+  }
   NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
                    c.stream));
   if (with_loss)
@@ -736,18 +937,21 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
                      c.comm, c.stream));
   NK(ncclGroupEnd());
   if (after_comm) CK(cudaEventRecord(after_comm, c.stream));
-  AdamArgs a = adam_args(c);
+  const StepStats *guard = nullptr;
   if (probe) {
-    // probe this rank's shard of the table and the (replicated) MLP, then
-    // combine over the ranks so every rank takes the same decision
-    AdamArgs ap = a;
-    ap.hash_count = shard;
-    launch_numerics_probe(ap, c.params.p + off, c.m.p + off, c.v.p + off,
-                          c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
-                          c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
-                          c.hash_count - off, c.stats(), 1, gate ? 1 : 0,
-                          c.num_sms, c.stream);
-    c.launches++;
+    AdamArgs a = adam_args(c);
+    for (size_t i = 0; i < bs.size(); ++i) {
+      const uint64_t gs = bs[i].n / c.world, off = bs[i].e0 + gs * c.rank;
+      AdamArgs ap = a;
+      ap.hash_count = gs;
+      if (i > 0) ap.mlp_count = 0;  // the MLP is scanned once
+      launch_numerics_probe(ap, c.params.p + off, c.m.p + off, c.v.p + off,
+                            c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
+                            c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                            c.hash_count - off, c.stats(), 1, gate ? 1 : 0,
+                            c.num_sms, c.stream);
+      c.launches++;
+    }
     StepStats *st = c.stats();
     NK(ncclGroupStart());
     NK(ncclAllReduce(&st->grad_l2, &st->grad_l2, 1, ncclFloat64, ncclSum,
@@ -755,57 +959,31 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
     NK(ncclAllReduce(&st->max_abs_grad, &st->max_abs_grad, 4, ncclFloat32,
                      ncclMax, c.comm, c.stream));
     NK(ncclGroupEnd());
-    a.guard = st;
+    guard = st;
   }
-  AdamArgs ah = a;
-  ah.hash_count = shard;
-  ah.slots = sslots;
-  ah.mlp_count = 0;
-  launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
-              c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
-              c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
-              c.touched.p + soff, c.table_h.p ? c.table_h.p + off : nullptr,
-              c.num_sms, c.stream);
-  launch_adam_mlp(a, c.params.p, c.m.p, c.v.p, c.gm.p, c.num_sms, c.stream);
-  c.launches += 2;
-  // other ranks' partial sums outside this rank's shard
-  if (c.gh_fixed.p)
-    CK(cudaMemsetAsync(c.gh_fixed.p, 0, c.gh_fixed.bytes(), c.stream));
-  if (c.gh_float.p)
-    CK(cudaMemsetAsync(c.gh_float.p, 0, c.gh_float.bytes(), c.stream));
-  CK(cudaMemsetAsync(c.touched.p, 0, c.touched.bytes(), c.stream));
-  if (c.tensor_core_family() && c.table_h.p) {
-    // the fused kernels read only the fp16 gather copy of the table: gather
-    // that (half the bytes); the fp32 master stays sharded until synced
-    NK(ncclAllGather(c.table_h.p + off, c.table_h.p, shard, ncclHalf, c.comm,
-                     c.stream));
-  } else {
-    NK(ncclAllGather(c.params.p + off, c.params.p, shard, ncclFloat32, c.comm,
-                     c.stream));
-    if (c.table_h.p) {
-      launch_to_half(c.params.p, c.table_h.p, c.hash_count, c.num_sms,
-                     c.stream);
-      c.launches++;
-    }
-  }
-  c.stale = true;
-  fused_weights_changed(c.fws);
-  c.step++;
+  dp_finish_sharded(c, bs, guard);
 }
 
 // Collective (every rank): gathers the shards of the fp32 table, m and v so
 // every rank holds the full, current state again.
 void dp_sync_state(tmnn_ctx &c) {
   if (!c.stale) return;
-  const size_t shard = c.hash_count / c.world, off = shard * c.rank;
+  const uint64_t per = (uint64_t)c.nd.T * c.nd.F;
   NK(ncclGroupStart());
-  NK(ncclAllGather(c.params.p + off, c.params.p, shard, ncclFloat32, c.comm,
-                   c.stream));
-  NK(ncclAllGather(c.m.p + off, c.m.p, shard, ncclFloat32, c.comm, c.stream));
-  NK(ncclAllGather(c.v.p + off, c.v.p, shard, ncclFloat32, c.comm, c.stream));
+  for (const auto &r : c.stale_layout) {
+    const uint64_t e0 = per * r.first, n = per * (uint64_t)(r.second - r.first);
+    const uint64_t gs = n / c.world, off = e0 + gs * c.rank;
+    NK(ncclAllGather(c.params.p + off, c.params.p + e0, gs, ncclFloat32,
+                     c.comm, c.stream));
+    NK(ncclAllGather(c.m.p + off, c.m.p + e0, gs, ncclFloat32, c.comm,
+                     c.stream));
+    NK(ncclAllGather(c.v.p + off, c.v.p + e0, gs, ncclFloat32, c.comm,
+                     c.stream));
+  }
   NK(ncclGroupEnd());
   CK(cudaStreamSynchronize(c.stream));
   c.stale = false;
+  c.stale_layout.clear();
 }
 
 void require_synced(const tmnn_ctx &c, const char *what) {
@@ -895,10 +1073,40 @@ void activate_safe_family(tmnn_ctx &c) {
 void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
               float inv_N, bool prof, bool force, bool gate) {
   CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(StepStats), c.stream));
+  // Bucketed exchange behind the level-major scatter (Tiled family, data
+  // parallel).  Probed steps take the plain path below: their probe reads
+  // the reduced gradients of every bucket before any update.
+  const bool shard = can_shard(c);
+  std::vector<Bucket> bs;
+  if (can_overlap(c) && !force) {
+    bs = shard ? shard_layout(c) : dp_bucket_list(c);
+    if (bs.size() < 2) bs.clear();
+  }
+  if (!bs.empty()) {
+    if (shard && c.stale && !layout_is(c, bs)) dp_sync_state(c);
+    if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
+    fwd_bwd_overlapped(c, p, t, N, inv_N, shard, true, bs);
+    if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
+    join_exchange(c);
+    if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
+    if (shard) {
+      dp_finish_sharded(c, bs);
+    } else {
+      probe_numerics(c, false, gate);
+      adam(c, c.stats());
+    }
+    if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
+    CK(cudaMemcpyAsync(c.h_stats, c.loss_acc.p, sizeof(StepStats),
+                       cudaMemcpyDeviceToHost, c.stream));
+    if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
+    CK(cudaStreamSynchronize(c.stream));
+    CK(cudaGetLastError());
+    return;
+  }
   if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
   fwd_bwd(c, p, t, nullptr, N, inv_N);
   if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
-  if (can_shard(c)) {
+  if (shard) {
     // sharded: the probe needs a cross-rank combine, so it runs only on
     // forced steps (sampled steps and every step of a recovery mode)
     dp_update(c, true, prof ? c.ev[3] : nullptr, force, gate);
@@ -1760,12 +1968,32 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
       ncclCommDestroy(c->comm);
       c->comm = nullptr;
     }
+    if (c->stale) throw std::invalid_argument(
+        "dp_init: call tmnn_cuda_dp_sync_state before re-initialising");
     c->rank = rank;
     c->world = world;
     if (world > 1) {
       ncclUniqueId id;
       std::memcpy(&id, unique_id, 128);
       NK(ncclCommInitRank(&c->comm, world, id, rank));
+      if (!c->comm_stream)
+        CK(cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking));
+      for (auto &e : c->dp_ev)
+        if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      if (const char *e = std::getenv("TMNN_DP_BUCKETS")) {
+        const int v = std::atoi(e);
+        if (v >= 1) c->dp_buckets = v;
+      }
+      // Under data parallelism the Tiled family (same per-point arithmetic
+      // as FullyFused) lets the gradient exchange overlap its level-major
+      // scatter; Auto switches to it when it can run the shape.
+      if (c->cfg.family == TMNN_FAMILY_AUTO &&
+          c->family == TMNN_FAMILY_FULLY_FUSED && c->dp_buckets > 1 &&
+          tiled_supported(c->nd, nullptr)) {
+        c->family = TMNN_FAMILY_TILED;
+        c->plan_text += "; data parallel: Tiled, so the gradient exchange "
+                        "overlaps the level-major scatter";
+      }
     }
   });
 }

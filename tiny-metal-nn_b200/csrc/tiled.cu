@@ -22,6 +22,7 @@
 //                    corners).
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -30,6 +31,16 @@
 
 namespace tmnn {
 namespace {
+
+// TMNN_TILED_PREFETCH=0 turns the next-level L2 prefetch off (for
+// measurements); default on.
+int prefetch_enabled() {
+  static const int on = [] {
+    const char *e = std::getenv("TMNN_TILED_PREFETCH");
+    return e && e[0] == '0' ? 0 : 1;
+  }();
+  return on;
+}
 
 constexpr int kThreads = 256;
 // Levels whose resolution is at most this are scattered with warp
@@ -48,8 +59,36 @@ struct TiledParams {
   uint8_t *touched;
   uint32_t N;
   uint32_t blocks_per_level;
+  int level0;  // level of the launch's first block (scatter of a level range)
   int implicit_touch;
+  int prefetch;  // stage the next level's slice into L2 ahead of its blocks
 };
+
+// Bulk prefetch of a contiguous byte range into L2 (TMA unit, no data
+// returned to the SM).  Address and size are multiples of 16 bytes.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p),
+               "r"(bytes)
+               : "memory");
+}
+
+// Block b of level l prefetches its 1/blocks_per_level share of level l+1's
+// slice of `base` (slice_bytes per level), so the next level's first
+// touches find their sectors in L2.
+__device__ __forceinline__ void prefetch_next_level(const TiledParams &P,
+                                                    const void *base,
+                                                    uint64_t slice_bytes,
+                                                    int l, int levels) {
+  if (!P.prefetch || threadIdx.x != 0 || l + 1 >= levels) return;
+  const uint64_t chunk =
+      ((slice_bytes + P.blocks_per_level - 1) / P.blocks_per_level + 15) & ~15ull;
+  const uint64_t start = (uint64_t)(blockIdx.x % P.blocks_per_level) * chunk;
+  if (start >= slice_bytes) return;
+  const uint64_t n = slice_bytes - start < chunk ? slice_bytes - start : chunk;
+  prefetch_l2(reinterpret_cast<const uint8_t *>(base) +
+                  (uint64_t)(l + 1) * slice_bytes + start,
+              (uint32_t)n);
+}
 
 // Scalar loads: positions may be a caller's device array with 4-byte
 // alignment only.
@@ -65,6 +104,10 @@ __global__ void __launch_bounds__(kThreads)
     k_tiled_encode(const __grid_constant__ TiledParams P) {
   const NetDims &nd = P.nd;
   const int l = (int)(blockIdx.x / P.blocks_per_level);
+  if (HALF)
+    prefetch_next_level(P, P.table16, (uint64_t)nd.T * F * 2, l, nd.L);
+  else
+    prefetch_next_level(P, P.table32, (uint64_t)nd.T * F * 4, l, nd.L);
   const uint32_t i =
       (blockIdx.x % P.blocks_per_level) * kThreads + threadIdx.x;
   if (i >= P.N) return;
@@ -107,8 +150,12 @@ __global__ void __launch_bounds__(kThreads)
     k_tiled_scatter(const __grid_constant__ TiledParams P) {
   __shared__ float stage[kThreads / 32][64];
   const NetDims &nd = P.nd;
-  const int l = (int)(blockIdx.x / P.blocks_per_level);
+  const int l = P.level0 + (int)(blockIdx.x / P.blocks_per_level);
   if (l >= nd.active_levels) return;  // uniform over the block
+  if (nd.grad_fixed)
+    prefetch_next_level(P, P.gh_fixed, (uint64_t)nd.T * F * 4, l, nd.active_levels);
+  else
+    prefetch_next_level(P, P.gh_float, (uint64_t)nd.T * F * 4, l, nd.active_levels);
   const uint32_t i =
       (blockIdx.x % P.blocks_per_level) * kThreads + threadIdx.x;
   const bool valid = i < P.N;
@@ -251,6 +298,7 @@ int tiled_encode(const NetDims &nd, const float *table32,
   P.table16 = table16;
   P.feat = feat;
   P.N = N;
+  P.prefetch = prefetch_enabled();
   P.blocks_per_level = (N + kThreads - 1) / kThreads;
   fn<<<P.blocks_per_level * (uint32_t)nd.L, kThreads, 0, st>>>(P);
   return 1;
@@ -258,8 +306,12 @@ int tiled_encode(const NetDims &nd, const float *table32,
 
 int tiled_scatter(const NetDims &nd, const float *pos, const float *dfeat,
                   int32_t *gh_fixed, float *gh_float, uint8_t *touched,
-                  uint32_t N, bool implicit_touch, cudaStream_t st) {
-  if (N == 0 || nd.active_levels <= 0) return 0;
+                  uint32_t N, bool implicit_touch, cudaStream_t st, int l0,
+                  int l1) {
+  const int active = nd.active_levels < nd.L ? nd.active_levels : nd.L;
+  if (l1 < 0 || l1 > active) l1 = active;
+  if (l0 < 0) l0 = 0;
+  if (N == 0 || l1 <= l0) return 0;
   TiledFn fn = pick_scatter(nd.d, nd.F);
   if (!fn) throw std::runtime_error("tiled: no scatter kernel for this shape");
   TiledParams P{};
@@ -271,9 +323,10 @@ int tiled_scatter(const NetDims &nd, const float *pos, const float *dfeat,
   P.touched = touched;
   P.N = N;
   P.implicit_touch = implicit_touch ? 1 : 0;
+  P.prefetch = prefetch_enabled();
   P.blocks_per_level = (N + kThreads - 1) / kThreads;
-  const int levels = nd.active_levels < nd.L ? nd.active_levels : nd.L;
-  fn<<<P.blocks_per_level * (uint32_t)levels, kThreads, 0, st>>>(P);
+  P.level0 = l0;
+  fn<<<P.blocks_per_level * (uint32_t)(l1 - l0), kThreads, 0, st>>>(P);
   return 1;
 }
 

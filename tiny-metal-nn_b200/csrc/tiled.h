@@ -36,9 +36,13 @@ int tiled_encode(const NetDims &nd, const float *table32,
 // point x 2^16, truncated) or gh_float (vector float reductions), marking
 // touched slots unless implicit_touch (float gradients: a nonzero sum marks
 // the slot).  Levels >= nd.active_levels receive nothing.
+// Levels [l0, l1) only (l1 < 0: up to the active levels), so that a
+// data-parallel step can exchange a finished group of levels while the next
+// group is being scattered.
 int tiled_scatter(const NetDims &nd, const float *pos, const float *dfeat,
                   int32_t *gh_fixed, float *gh_float, uint8_t *touched,
-                  uint32_t N, bool implicit_touch, cudaStream_t st);
+                  uint32_t N, bool implicit_touch, cudaStream_t st, int l0 = 0,
+                  int l1 = -1);
 
 // One training pass: encode, MLP forward + loss (tgt) or the caller's
 // dL/dy (dext) + backward (weight gradients into gm, summed loss into
