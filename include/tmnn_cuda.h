@@ -118,7 +118,8 @@ typedef struct tmnn_train_cfg {
                                       one allreduce; 0 (default): from 4
                                       ranks on, Adam is sharded over the
                                       ranks (reduce-scatter, Adam on 1/world
-                                      of the table, all-gather) */
+                                      of the table, all-gather); -1: sharded
+                                      from 2 ranks on */
   /* numerics guard (RuntimePolicy, include/tiny-metal-nn/runtime_policy.h:
    * 13-40; defaults from TMNN_NUMERICS_SAMPLING_MODE,
    * TMNN_NUMERICS_SAMPLE_INTERVAL, TMNN_BAD_STEP_MODE like

@@ -10,7 +10,8 @@ LOSS_NAMES = {0: "L2", 1: "L1", 2: "Huber", 3: "Cosine"}
 def cuda_trainer(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=0, base=16.0,
                  scale=1.447, huber=1.0, family="SafeDebug", grad="Fixed16",
                  table="F32", morton=True, seed=42, lr_enc=1e-2, lr_net=1e-3,
-                 l1=0.0, l2=0.0, batch=1024, sparse=None, device=0):
+                 l1=0.0, l2=0.0, batch=1024, sparse=None, device=0,
+                 cfg_extra=None):
     import tmnn_b200 as t
     from tmnn_b200 import _abi
     spec = _abi.Spec(L, F, log2T, d, base, scale, W, H, O, loss, huber,
@@ -28,6 +29,8 @@ def cuda_trainer(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=0, base=16.0,
     cfg.batch_size = batch
     if sparse is not None:
         cfg.sparse_hash_adam = 1 if sparse else 0
+    for k, v in (cfg_extra or {}).items():
+        setattr(cfg, k, v)
     return t.Trainer.from_spec(spec, cfg, device=device)
 
 

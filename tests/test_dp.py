@@ -105,7 +105,7 @@ def test_dp_design_matches_single_process_gloo(steps):
     assert np.allclose(res[0][hw.size:], w[hw.size:], rtol=1e-4, atol=1e-6)
 
 
-def _gpu_rank(rank, world, port, q, family, grad):
+def _gpu_rank(rank, world, port, q, family, grad, extra=None):
     import sys
     for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),
               os.path.join(ROOT, "oracle")):
@@ -117,7 +117,7 @@ def _gpu_rank(rank, world, port, q, family, grad):
     import tmnn_b200 as t
     from _util import cuda_trainer
     kw = KW_FUSED if family != "SafeDebug" else KW
-    tr = cuda_trainer(**kw, family=family, grad=grad, device=rank)
+    tr = cuda_trainer(**kw, family=family, grad=grad, device=rank, cfg_extra=extra)
     uid = [t.dp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     tr.dp_init(uid[0], rank, world)
@@ -134,16 +134,19 @@ def _gpu_rank(rank, world, port, q, family, grad):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("family,grad", [("SafeDebug", "Fixed16"), ("FullyFused", "F32"),
-                                         ("Tiled", "F32"), ("Tiled", "Fixed16")])
-def test_dp_nccl_two_gpus_match_one(family, grad):
+@pytest.mark.parametrize("family,grad,sharded", [
+    ("SafeDebug", "Fixed16", False), ("FullyFused", "F32", False),
+    ("Tiled", "F32", False), ("Tiled", "Fixed16", False),
+    ("Tiled", "F32", True), ("FullyFused", "Fixed16", True)])
+def test_dp_nccl_two_gpus_match_one(family, grad, sharded):
     """N ranks (4 when the box has them: the sharded optimizer; else 2: the
     allreduce) on slices of each batch against one process on the whole
     batch.  The Tiled family exchanges its gradients bucket by bucket behind
     the level-major scatter.  Float gradients sum in a different order, and
     Adam moves a slot by about lr whatever its gradient's size, so the float
     runs compare weight changes by direction (cosine); fixed-point runs
-    compare values."""
+    compare values.  `sharded` forces the sharded optimizer from 2 ranks on
+    (dp_replicated_optimizer = -1)."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 4 if torch.cuda.device_count() >= 4 else 2  # 4: sharded optimizer
@@ -151,7 +154,8 @@ def test_dp_nccl_two_gpus_match_one(family, grad):
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_gpu_rank, args=(r, world, port, q, family, grad))
+    extra = {"dp_replicated_optimizer": -1} if sharded else None
+    procs = [ctx.Process(target=_gpu_rank, args=(r, world, port, q, family, grad, extra))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -181,3 +185,86 @@ def test_dp_nccl_two_gpus_match_one(family, grad):
         assert cos(h0 - hi, hr - hi) >= 0.999
         assert cos(m0 - mi, mr - mi) >= 0.999
     ref.close()
+
+
+def _retry_rank(rank, world, port, q):
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),
+              os.path.join(ROOT, "oracle")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import tmnn_b200 as t
+    tr = _retry_trainer(rank)
+    uid = [t.dp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    tr.dp_init(uid[0], rank, world)
+    init = tr.weights()
+    pos, tgt = _data(steps=1)[0]
+    n = pos.shape[0] // world
+    loss = tr.training_step(np.ascontiguousarray(pos[rank * n:(rank + 1) * n]),
+                            np.ascontiguousarray(tgt[rank * n:(rank + 1) * n]))
+    action = tr.last_numerics()["recovery_action"]
+    tr.dp_sync_state()
+    q.put((rank, tr.weights(), loss, action, init))
+    tr.close()
+    dist.destroy_process_group()
+
+
+def _retry_trainer(device):
+    """FullyFused trainer whose table holds values above the fp16 range: the
+    tensor-core step overflows, the fp32 SafeDebug retry does not."""
+    from _util import cuda_trainer
+    from tmnn_b200 import _abi
+    tr = cuda_trainer(**KW_FUSED, family="FullyFused", grad="F32", device=device,
+                      cfg_extra={"dp_replicated_optimizer": -1,
+                                 "bad_step_recovery":
+                                     _abi.BAD_STEP["FallbackAndRetryWithSafeFamily"]})
+    hw, mw = tr.weights()
+    tr.set_initial_weights(np.full_like(hw, 6.0e4), np.abs(mw) + 0.05)
+    return tr
+
+
+@pytest.mark.gpu
+def test_dp_sharded_safe_family_retry_matches_one_process():
+    """FallbackAndRetryWithSafeFamily under the sharded optimizer: the fp32
+    master outside a rank's shard is out of date after a sharded step, and
+    the SafeDebug retry reads it, so the runtime gathers it first.  Two ranks
+    (sharding forced) against one process on the whole batch."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_retry_rank, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, wts, loss, action, init = q.get(timeout=120)
+        res[r] = (wts, loss, action, init)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = _retry_trainer(0)
+    pos, tgt = _data(steps=1)[0]
+    lr = ref.training_step(pos, tgt)
+    assert ref.last_numerics()["recovery_action"] == "RetriedWithSafeFamily"
+    hr, mr = ref.weights()
+    ref.close()
+    (h0, m0), l0, a0, (hi, mi) = res[0]
+    (h1, m1), _, a1, _ = res[1]
+    assert a0 == a1 == "RetriedWithSafeFamily"
+    assert np.array_equal(h0, h1) and np.array_equal(m0, m1)
+    assert np.isfinite(h0).all() and np.isfinite(m0).all()
+    assert abs(l0 - lr) <= 1e-3 * abs(lr)
+
+    def cos(a, b):
+        a, b = a.astype(np.float64), b.astype(np.float64)
+        return a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300)
+    assert cos(h0 - hi, hr - hi) >= 0.999
+    assert cos(m0 - mi, mr - mi) >= 0.999

@@ -171,7 +171,12 @@ struct tmnn_ctx {
   // bucketed exchange (Tiled family): the gradient collectives run on
   // comm_stream, one bucket of levels at a time, behind the scatter
   cudaStream_t comm_stream = nullptr;
+  // [0] MLP done, [1 + g] bucket g scattered, [kMaxLevels + 1] exchange
+  // done (main stream); ev_comm[g] bucket g reduced, ev_comm[kMaxLevels]
+  // MLP/loss reduced (comm stream); ev_adam[g] bucket g updated
   cudaEvent_t dp_ev[kMaxLevels + 2] = {};
+  cudaEvent_t ev_comm[kMaxLevels + 1] = {};
+  cudaEvent_t ev_adam[kMaxLevels + 1] = {};
   int dp_buckets = 4;
   int rank = 0, world = 1;
   // sharded data-parallel optimizer: this rank's copies of the fp32 table
@@ -200,6 +205,10 @@ struct tmnn_ctx {
       cudaStreamDestroy(comm_stream);
     }
     for (auto e : dp_ev)
+      if (e) cudaEventDestroy(e);
+    for (auto e : ev_comm)
+      if (e) cudaEventDestroy(e);
+    for (auto e : ev_adam)
       if (e) cudaEventDestroy(e);
     if (h_stats) cudaFreeHost(h_stats);
     for (auto e : ev)
@@ -723,7 +732,8 @@ void adam(tmnn_ctx &c, const StepStats *guard = nullptr) {
 bool can_shard(const tmnn_ctx &c) {
   // at 2 ranks the extra memsets and fp16 refresh cost more than the halved
   // Adam saves (measured); from 4 ranks on the sharded update is cheaper
-  return c.comm && c.world >= 4 && c.cfg.dp_replicated_optimizer == 0 &&
+  return c.comm && c.cfg.dp_replicated_optimizer <= 0 &&
+         (c.world >= 4 || (c.world >= 2 && c.cfg.dp_replicated_optimizer < 0)) &&
          c.hash_count % (4ull * (uint64_t)c.world) == 0 &&
          c.slots % (uint64_t)c.world == 0;
 }
@@ -771,66 +781,131 @@ bool buckets_shardable(const tmnn_ctx &c, const std::vector<Bucket> &bs) {
   return true;
 }
 
-void fwd_bwd_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
-                        uint32_t N, float inv_N, bool shard, bool with_loss,
-                        const std::vector<Bucket> &bs) {
+// One data-parallel training pass of the Tiled family, pipelined per bucket
+// of levels over two streams:
+//
+//   main:  encode, MLP | scatter b0 | scatter b1 | ... | Adam MLP |
+//          Adam b0 | Adam b1 | ...
+//   comm:  MLP + loss allreduce | reduce b0 | reduce b1 | ... |
+//          all-gather b0 | all-gather b1 | ...
+//
+// Bucket g's reduction (a reduce-scatter with the sharded optimizer, else an
+// allreduce) starts when its scatter is done and overlaps the later
+// buckets' scatter; its Adam starts when its reduction is done, and (sharded)
+// its all-gather when its Adam is done.  The main stream joins the comm
+// stream at the end, so the next step sees a complete table.
+void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
+                     uint32_t N, float inv_N, bool shard, bool gate,
+                     const std::vector<Bucket> &bs, bool prof) {
   const NetDims &nd = c.nd;
   const bool fixed = nd.grad_fixed != 0;
   const bool exch_touched = c.sparse && !c.implicit_touch;
+  const uint64_t w = (uint64_t)c.entry_width;
+  cudaStream_t cs = c.comm_stream;
   c.launches += tiled_encode(nd, c.params.p, c.gather_half(), pos, c.feat.p, N,
                              c.stream);
   c.launches += fused_mlp_train(c.fws, nd, c.mlp_w(), c.feat.p, tgt, nullptr,
                                 inv_N, c.gm.p, c.loss_acc.p, c.dfeat.p, N,
                                 c.num_sms, c.stream, 0);
   CK(cudaEventRecord(c.dp_ev[0], c.stream));
-  CK(cudaStreamWaitEvent(c.comm_stream, c.dp_ev[0], 0));
+  CK(cudaStreamWaitEvent(cs, c.dp_ev[0], 0));
   NK(ncclGroupStart());
-  NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
-                   c.comm_stream));
-  if (with_loss)
-    NK(ncclAllReduce(c.loss_acc.p, c.loss_acc.p, 1, ncclFloat64, ncclSum,
-                     c.comm, c.comm_stream));
+  NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm, cs));
+  NK(ncclAllReduce(c.loss_acc.p, c.loss_acc.p, 1, ncclFloat64, ncclSum, c.comm, cs));
   NK(ncclGroupEnd());
+  CK(cudaEventRecord(c.ev_comm[kMaxLevels], cs));
   for (size_t g = 0; g < bs.size(); ++g) {
     const Bucket &b = bs[g];
     c.launches += tiled_scatter(nd, pos, c.dfeat.p, c.gh_fixed.p, c.gh_float.p,
                                 c.touched.p, N, c.implicit_touch, c.stream,
                                 b.l0, b.l1);
     CK(cudaEventRecord(c.dp_ev[1 + g], c.stream));
-    CK(cudaStreamWaitEvent(c.comm_stream, c.dp_ev[1 + g], 0));
-    const uint64_t w = (uint64_t)c.entry_width;
+    CK(cudaStreamWaitEvent(cs, c.dp_ev[1 + g], 0));
     NK(ncclGroupStart());
     if (shard) {
       const uint64_t gs = b.n / c.world, own = b.e0 + gs * c.rank;
       if (fixed)
         NK(ncclReduceScatter(c.gh_fixed.p + b.e0, c.gh_fixed.p + own, gs,
-                             ncclInt32, ncclSum, c.comm, c.comm_stream));
+                             ncclInt32, ncclSum, c.comm, cs));
       else
         NK(ncclReduceScatter(c.gh_float.p + b.e0, c.gh_float.p + own, gs,
-                             ncclFloat32, ncclSum, c.comm, c.comm_stream));
+                             ncclFloat32, ncclSum, c.comm, cs));
       if (exch_touched)
         NK(ncclReduceScatter(c.touched.p + b.e0 / w, c.touched.p + own / w,
-                             gs / w, ncclUint8, ncclMax, c.comm,
-                             c.comm_stream));
+                             gs / w, ncclUint8, ncclMax, c.comm, cs));
     } else {
       if (fixed)
         NK(ncclAllReduce(c.gh_fixed.p + b.e0, c.gh_fixed.p + b.e0, b.n,
-                         ncclInt32, ncclSum, c.comm, c.comm_stream));
+                         ncclInt32, ncclSum, c.comm, cs));
       else
         NK(ncclAllReduce(c.gh_float.p + b.e0, c.gh_float.p + b.e0, b.n,
-                         ncclFloat32, ncclSum, c.comm, c.comm_stream));
+                         ncclFloat32, ncclSum, c.comm, cs));
       if (exch_touched)
         NK(ncclAllReduce(c.touched.p + b.e0 / w, c.touched.p + b.e0 / w,
-                         b.n / w, ncclUint8, ncclMax, c.comm, c.comm_stream));
+                         b.n / w, ncclUint8, ncclMax, c.comm, cs));
     }
     NK(ncclGroupEnd());
+    CK(cudaEventRecord(c.ev_comm[g], cs));
   }
-  CK(cudaEventRecord(c.dp_ev[kMaxLevels + 1], c.comm_stream));
-}
-
-// The main stream waits for the last collective of fwd_bwd_overlapped.
-void join_exchange(tmnn_ctx &c) {
-  CK(cudaStreamWaitEvent(c.stream, c.dp_ev[kMaxLevels + 1], 0));
+  if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
+  // MLP update (and, replicated, the unforced numerics check of the loss)
+  CK(cudaStreamWaitEvent(c.stream, c.ev_comm[kMaxLevels], 0));
+  AdamArgs a = adam_args(c);
+  if (!shard) {
+    probe_numerics(c, false, gate);
+    a.guard = c.stats();
+  }
+  launch_adam_mlp(a, c.params.p, c.m.p, c.v.p, c.gm.p, c.num_sms, c.stream);
+  c.launches++;
+  const bool half = c.tensor_core_family() && c.table_h.p;
+  for (size_t g = 0; g < bs.size(); ++g) {
+    const Bucket &b = bs[g];
+    CK(cudaStreamWaitEvent(c.stream, c.ev_comm[g], 0));
+    if (prof && g + 1 == bs.size()) CK(cudaEventRecord(c.ev[3], c.stream));
+    const uint64_t gs = shard ? b.n / c.world : b.n;
+    const uint64_t off = shard ? b.e0 + gs * c.rank : b.e0;
+    AdamArgs ah = a;
+    ah.hash_count = gs;
+    ah.slots = gs / w;
+    ah.mlp_count = 0;
+    launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
+                c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
+                c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                c.touched.p + off / w, c.table_h.p ? c.table_h.p + off : nullptr,
+                c.num_sms, c.stream);
+    c.launches++;
+    if (shard) {
+      // the bucket's other ranks' partial sums (outside this rank's shard)
+      if (c.gh_fixed.p)
+        CK(cudaMemsetAsync(c.gh_fixed.p + b.e0, 0, b.n * 4, c.stream));
+      if (c.gh_float.p)
+        CK(cudaMemsetAsync(c.gh_float.p + b.e0, 0, b.n * 4, c.stream));
+      CK(cudaMemsetAsync(c.touched.p + b.e0 / w, 0, b.n / w, c.stream));
+      CK(cudaEventRecord(c.ev_adam[g], c.stream));
+      CK(cudaStreamWaitEvent(cs, c.ev_adam[g], 0));
+      if (half)
+        NK(ncclAllGather(c.table_h.p + off, c.table_h.p + b.e0, gs, ncclHalf,
+                         c.comm, cs));
+      else
+        NK(ncclAllGather(c.params.p + off, c.params.p + b.e0, gs, ncclFloat32,
+                         c.comm, cs));
+    } else if (!c.sparse) {
+      CK(cudaMemsetAsync(c.touched.p + b.e0 / w, 0, b.n / w, c.stream));
+    }
+  }
+  if (shard) {
+    CK(cudaEventRecord(c.dp_ev[kMaxLevels + 1], cs));
+    CK(cudaStreamWaitEvent(c.stream, c.dp_ev[kMaxLevels + 1], 0));
+    if (!half && c.table_h.p) {
+      launch_to_half(c.params.p, c.table_h.p, c.hash_count, c.num_sms, c.stream);
+      c.launches++;
+    }
+    c.stale = true;
+    c.stale_layout.clear();
+    for (const Bucket &b : bs) c.stale_layout.push_back({b.l0, b.l1});
+  }
+  fused_weights_changed(c.fws);
+  c.step++;
 }
 
 // Sharded update after a bucketed reduce-scatter: Adam on this rank's
@@ -1085,16 +1160,7 @@ void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
   if (!bs.empty()) {
     if (shard && c.stale && !layout_is(c, bs)) dp_sync_state(c);
     if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
-    fwd_bwd_overlapped(c, p, t, N, inv_N, shard, true, bs);
-    if (prof) CK(cudaEventRecord(c.ev[2], c.stream));
-    join_exchange(c);
-    if (prof) CK(cudaEventRecord(c.ev[3], c.stream));
-    if (shard) {
-      dp_finish_sharded(c, bs);
-    } else {
-      probe_numerics(c, false, gate);
-      adam(c, c.stats());
-    }
+    step_overlapped(c, p, t, N, inv_N, shard, gate, bs, prof);
     if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
     CK(cudaMemcpyAsync(c.h_stats, c.loss_acc.p, sizeof(StepStats),
                        cudaMemcpyDeviceToHost, c.stream));
@@ -1976,9 +2042,18 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
       ncclUniqueId id;
       std::memcpy(&id, unique_id, 128);
       NK(ncclCommInitRank(&c->comm, world, id, rank));
-      if (!c->comm_stream)
-        CK(cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking));
+      if (!c->comm_stream) {
+        // highest priority: the collectives' blocks are scheduled ahead of
+        // the pending blocks of the scatter they overlap
+        int lo = 0, hi = 0;
+        CK(cudaDeviceGetStreamPriorityRange(&lo, &hi));
+        CK(cudaStreamCreateWithPriority(&c->comm_stream, cudaStreamNonBlocking, hi));
+      }
       for (auto &e : c->dp_ev)
+        if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      for (auto &e : c->ev_comm)
+        if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      for (auto &e : c->ev_adam)
         if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
       if (const char *e = std::getenv("TMNN_DP_BUCKETS")) {
         const int v = std::atoi(e);
