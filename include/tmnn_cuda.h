@@ -262,6 +262,24 @@ tmnn_status tmnn_cuda_train_step(tmnn_ctx *ctx, const float *positions,
                                  const float *targets, uint32_t n,
                                  uint32_t flags, tmnn_step_result *result);
 
+/* Pipelined training steps (enqueue_training_step / finalize_training_step,
+ * src/tiny_metal_nn/runtime/training_step_execution.cpp:887-1235, over the
+ * two step lanes of default_trainer.cpp:41).  _enqueue copies the batch into
+ * one of two device lanes on a copy stream and queues the step behind it;
+ * it returns without waiting.  _finalize waits for the oldest pending step
+ * and fills *result (the same fields as tmnn_cuda_train_step).  At most two
+ * steps may be pending; with two in flight the upload of one batch overlaps
+ * the other's kernels.  Host arrays must stay unchanged until their step is
+ * finalized; pinned host memory makes the copy asynchronous.  Numerics
+ * recovery modes other than SignalOnly are refused (they need the host
+ * between steps); tmnn_cuda_train_step refuses to run while steps are
+ * pending. */
+tmnn_status tmnn_cuda_train_step_enqueue(tmnn_ctx *ctx, const float *positions,
+                                         const float *targets, uint32_t n,
+                                         uint32_t flags);
+tmnn_status tmnn_cuda_train_step_finalize(tmnn_ctx *ctx,
+                                          tmnn_step_result *result);
+
 /* The forward/backward half of training_step without the optimizer: Morton
  * sort, fused forward/backward/scatter with the internal loss, gradients
  * ACCUMULATED into the gradient buffers (the command batch that

@@ -116,13 +116,17 @@ def test_tiled_ragged_batches(N):
     b.close()
 
 
-def test_auto_selects_tiled_when_tables_overflow_l2():
+def test_auto_selects_tiled_when_tables_take_a_quarter_of_l2():
     big = cuda_trainer(L=16, F=2, log2T=22, d=4, W=64, H=2, O=4, loss=0,
                        base=8.0, scale=1.5, family="Auto", table="F16",
                        grad="F32")
     assert big.plan()["family"] == "Tiled", big.plan()
     big.close()
-    small = cuda_trainer(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=1,
-                         family="Auto", table="F16", grad="F32")
+    mid = cuda_trainer(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=1,
+                       family="Auto", table="F16", grad="F32")
+    assert mid.plan()["family"] == "Tiled", mid.plan()
+    mid.close()
+    small = cuda_trainer(L=16, F=2, log2T=15, d=3, W=64, H=2, O=3, loss=0,
+                         scale=1.5, family="Auto", table="F32", grad="F32")
     assert small.plan()["family"] == "FullyFused", small.plan()
     small.close()

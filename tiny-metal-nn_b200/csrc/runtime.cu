@@ -165,6 +165,19 @@ struct tmnn_ctx {
   bool safe_family_active = false;
   StepStats *stats() { return reinterpret_cast<StepStats *>(loss_acc.p); }
   cudaEvent_t ev[6] = {};
+  // two-lane step ring of the enqueue / finalize API: each lane holds its
+  // batch's device copy of the inputs and its pinned step statistics, so the
+  // upload of step k+1 overlaps the device work of step k
+  struct StepLane {
+    DevBuf<float> pos, tgt;
+    StepStats *h_stats = nullptr;
+    cudaEvent_t copied = nullptr, consumed = nullptr, done = nullptr;
+    uint32_t N = 0, step = 0;
+    bool used = false;
+  };
+  StepLane lanes[2];
+  int lane_next = 0, lane_oldest = 0, n_pending = 0;
+  cudaStream_t copy_stream = nullptr;
   FusedWorkspace fws;
   // data parallelism
   ncclComm_t comm = nullptr;
@@ -211,6 +224,15 @@ struct tmnn_ctx {
     for (auto e : ev_adam)
       if (e) cudaEventDestroy(e);
     if (h_stats) cudaFreeHost(h_stats);
+    for (auto &l : lanes) {
+      if (l.h_stats) cudaFreeHost(l.h_stats);
+      for (cudaEvent_t e : {l.copied, l.consumed, l.done})
+        if (e) cudaEventDestroy(e);
+    }
+    if (copy_stream) {
+      cudaStreamSynchronize(copy_stream);
+      cudaStreamDestroy(copy_stream);
+    }
     for (auto e : ev)
       if (e) cudaEventDestroy(e);
     fused_release(fws);
@@ -398,8 +420,9 @@ NetDims make_dims(const tmnn_spec &s, const tmnn_train_cfg &c) {
 // NetworkPlanner::plan_with_capabilities (network_planner.cpp:132-290):
 // forced families win; Auto takes FullyFused when its kernel supports the
 // shape, except that when the table's gather copy plus its fp32 gradients
-// exceed the L2 the level-major Tiled family is selected (the fused
-// kernel's point-major gathers and reductions would go to HBM).  When the
+// take more than a quarter of the L2 the level-major Tiled family is
+// selected (the fused kernel's point-major gathers and reductions then
+// spill out of L2, or compete for it).  When the
 // tensor-core kernels cannot run the shape at all, SafeDebug (fp32 CUDA
 // cores) runs it, with the reason recorded and a warning on stderr.
 void plan_family(tmnn_ctx &c) {
@@ -411,7 +434,10 @@ void plan_family(tmnn_ctx &c) {
   cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, c.device);
   const uint64_t tbytes = c.spec.table_dtype == TMNN_DTYPE_F16 ? 2 : 4;
   const uint64_t resident = c.nd.hash_count * (tbytes + 4);
-  const bool overflows_l2 = l2 > 0 && resident > (uint64_t)l2;
+  // measured: the level-major family wins once table + gradients take more
+  // than a quarter of the L2 (sdf3d, 100 MB: fwd/bwd 0.303 against 0.322 ms)
+  // and loses on small tables (image, 8 MB: 0.365 against 0.325 ms)
+  const bool overflows_l2 = l2 > 0 && resident > (uint64_t)l2 / 4;
   auto fallback_reason = [](const std::string &w) {
     return w.find("hidden") != std::string::npos   ? kReasonHiddenDimUnsupported
            : w.find("output") != std::string::npos ? kReasonUnsupportedOutputDims
@@ -438,8 +464,8 @@ void plan_family(tmnn_ctx &c) {
     c.family = TMNN_FAMILY_TILED;
     c.fallback_reason = kReasonNone;
     c.plan_text = "Tiled: gather table + gradients (" +
-                  std::to_string(resident >> 20) + " MiB) exceed the L2 (" +
-                  std::to_string((uint64_t)l2 >> 20) +
+                  std::to_string(resident >> 20) + " MiB) exceed a quarter "
+                  "of the L2 (" + std::to_string((uint64_t)l2 >> 20) +
                   " MiB): level-major encode and scatter";
   } else if (fused_ok) {
     c.family = TMNN_FAMILY_FULLY_FUSED;
@@ -1145,8 +1171,9 @@ void activate_safe_family(tmnn_ctx &c) {
 // One forward/backward + update of an already staged (and sorted) batch,
 // ending with the read-back of the step statistics.  `force` probes the
 // gradients whatever the loss; `gate` lets an anomaly veto the update.
-void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
-              float inv_N, bool prof, bool force, bool gate) {
+void enqueue_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
+                  float inv_N, bool prof, bool force, bool gate,
+                  StepStats *host_stats) {
   CK(cudaMemsetAsync(c.loss_acc.p, 0, sizeof(StepStats), c.stream));
   // Bucketed exchange behind the level-major scatter (Tiled family, data
   // parallel).  Probed steps take the plain path below: their probe reads
@@ -1162,11 +1189,9 @@ void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
     if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
     step_overlapped(c, p, t, N, inv_N, shard, gate, bs, prof);
     if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
-    CK(cudaMemcpyAsync(c.h_stats, c.loss_acc.p, sizeof(StepStats),
+    CK(cudaMemcpyAsync(host_stats, c.loss_acc.p, sizeof(StepStats),
                        cudaMemcpyDeviceToHost, c.stream));
     if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
-    CK(cudaStreamSynchronize(c.stream));
-    CK(cudaGetLastError());
     return;
   }
   if (prof) CK(cudaEventRecord(c.ev[1], c.stream));
@@ -1183,9 +1208,16 @@ void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
     adam(c, c.stats());
   }
   if (prof) CK(cudaEventRecord(c.ev[4], c.stream));
-  CK(cudaMemcpyAsync(c.h_stats, c.loss_acc.p, sizeof(StepStats),
+  CK(cudaMemcpyAsync(host_stats, c.loss_acc.p, sizeof(StepStats),
                      cudaMemcpyDeviceToHost, c.stream));
   if (prof) CK(cudaEventRecord(c.ev[5], c.stream));
+}
+
+// One step's device work followed by the read-back of its statistics into
+// c.h_stats and a host wait.
+void run_step(tmnn_ctx &c, const float *p, const float *t, uint32_t N,
+              float inv_N, bool prof, bool force, bool gate) {
+  enqueue_step(c, p, t, N, inv_N, prof, force, gate, c.h_stats);
   CK(cudaStreamSynchronize(c.stream));
   CK(cudaGetLastError());
 }
@@ -1199,8 +1231,7 @@ struct StepReport {
   bool anomaly() const { return !ff || !fb || !fu; }
 };
 
-StepReport read_report(const tmnn_ctx &c, uint64_t global_n) {
-  const StepStats &h = *c.h_stats;
+StepReport read_report(const StepStats &h, uint64_t global_n) {
   StepReport r;
   // finalize_async_step: mean_loss = total / float(batch_N)
   // (parameter_store.cpp:303-322)
@@ -1237,6 +1268,9 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
                 uint32_t flags, tmnn_step_result *res) {
   if (N > 0 && (!pos || !tgt))
     throw std::invalid_argument("training_step: null positions or targets");
+  if (c.n_pending)
+    throw std::invalid_argument(
+        "training_step: enqueued steps are pending; finalize them first");
   CK(cudaSetDevice(c.device));
   ensure_batch(c, N);
   const bool prof = flags & TMNN_PROFILE;
@@ -1251,7 +1285,7 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
   const bool gate = mode != TMNN_BAD_STEP_SIGNAL_ONLY;
   const bool force = gate || c.guard.should_sample(done, false);
   run_step(c, p, t, N, inv_N, prof, force, gate);
-  StepReport rep = read_report(c, global_n);
+  StepReport rep = read_report(*c.h_stats, global_n);
   bool anomaly = rep.anomaly();
   bool reported = c.guard.should_sample(done, anomaly);
   if (reported) c.guard.record(done, anomaly);
@@ -1284,7 +1318,7 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
       // combined over the ranks), so the collective is matched.
       if (c.stale) dp_sync_state(c);
       run_step(c, p, t, N, inv_N, prof, true, true);
-      rep = read_report(c, global_n);
+      rep = read_report(*c.h_stats, global_n);
       anomaly = rep.anomaly();
       c.guard.record(done, anomaly);
       reported = true;
@@ -1322,6 +1356,105 @@ void train_step(tmnn_ctx &c, const float *pos, const float *tgt, uint32_t N,
       CK(cudaEventElapsedTime(&res->allreduce_ms, c.ev[2], c.ev[3]));
       CK(cudaEventElapsedTime(&res->adam_ms, c.ev[3], c.ev[4]));
     }
+  }
+}
+
+// Pipelined training steps (enqueue_training_step / finalize_training_step,
+// training_step_execution.cpp:887-1235, with the reference's two step lanes,
+// default_trainer.cpp:41): enqueue uploads the batch into a free lane on a
+// copy stream and queues the step's device work behind it without waiting;
+// finalize waits for the oldest pending step and reports it.  With two steps
+// in flight the host->device copy of one overlaps the other's kernels.  The
+// numerics probe is sampled as in training_step; recovery modes other than
+// SignalOnly need the host between steps and are refused here.
+void train_step_enqueue(tmnn_ctx &c, const float *pos, const float *tgt,
+                        uint32_t N, uint32_t flags) {
+  if (N > 0 && (!pos || !tgt))
+    throw std::invalid_argument("training_step_enqueue: null positions or targets");
+  if (c.cfg.bad_step_recovery != TMNN_BAD_STEP_SIGNAL_ONLY)
+    throw std::invalid_argument(
+        "training_step_enqueue: bad-step recovery modes need training_step");
+  if (c.n_pending >= 2)
+    throw std::invalid_argument(
+        "training_step_enqueue: two steps are pending; finalize one first");
+  CK(cudaSetDevice(c.device));
+  if (!c.copy_stream)
+    CK(cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking));
+  auto &L = c.lanes[c.lane_next];
+  if (!L.h_stats) {
+    CK(cudaMallocHost(&L.h_stats, sizeof(StepStats)));
+    for (cudaEvent_t *e : {&L.copied, &L.consumed, &L.done})
+      CK(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  }
+  ensure_batch(c, N);
+  const size_t np = (size_t)N * c.nd.d, nt = (size_t)N * c.nd.O;
+  const float *p = pos, *t = tgt;
+  if (!(flags & TMNN_PTR_DEVICE)) {
+    L.pos.ensure(np);
+    L.tgt.ensure(nt);
+    // the lane's previous batch must have been read before it is overwritten
+    if (L.used) CK(cudaStreamWaitEvent(c.copy_stream, L.consumed, 0));
+    if (np)
+      CK(cudaMemcpyAsync(L.pos.p, pos, np * sizeof(float),
+                         cudaMemcpyHostToDevice, c.copy_stream));
+    if (nt)
+      CK(cudaMemcpyAsync(L.tgt.p, tgt, nt * sizeof(float),
+                         cudaMemcpyHostToDevice, c.copy_stream));
+    CK(cudaEventRecord(L.copied, c.copy_stream));
+    CK(cudaStreamWaitEvent(c.stream, L.copied, 0));
+    p = L.pos.p;
+    t = L.tgt.p;
+  }
+  bool sorted = false;
+  if (c.cfg.morton_sort && N > 1) {
+    morton_sort(c, p, t, N, &p, &t);
+    sorted = true;
+    CK(cudaEventRecord(L.consumed, c.stream));
+  }
+  const uint64_t global_n = (uint64_t)N * (uint64_t)c.world;
+  const float inv_N = global_n ? 1.0f / (float)global_n : 0.0f;
+  L.step = c.step;
+  L.N = N;
+  const bool force = c.guard.should_sample(L.step, false);
+  enqueue_step(c, p, t, N, inv_N, false, force, false, L.h_stats);
+  if (!sorted) CK(cudaEventRecord(L.consumed, c.stream));
+  CK(cudaEventRecord(L.done, c.stream));
+  L.used = true;
+  c.lane_next ^= 1;
+  ++c.n_pending;
+}
+
+void train_step_finalize(tmnn_ctx &c, tmnn_step_result *res) {
+  if (c.n_pending == 0)
+    throw std::invalid_argument("training_step_finalize: no step is pending");
+  CK(cudaSetDevice(c.device));
+  auto &L = c.lanes[c.lane_oldest];
+  CK(cudaEventSynchronize(L.done));
+  CK(cudaGetLastError());
+  c.lane_oldest ^= 1;
+  --c.n_pending;
+  const uint64_t global_n = (uint64_t)L.N * (uint64_t)c.world;
+  const StepReport rep = read_report(*L.h_stats, global_n);
+  const bool anomaly = rep.anomaly();
+  const bool reported = c.guard.should_sample(L.step, anomaly);
+  if (reported) c.guard.record(L.step, anomaly);
+  if (res) {
+    std::memset(res, 0, sizeof *res);
+    res->loss = rep.mean_loss;
+    res->step = L.step;
+    res->batch_size = L.N;
+    res->numerics_ok = anomaly ? 0 : 1;
+    res->family = c.family;
+    res->grad_norm = rep.grad_norm;
+    res->finite_forward = rep.ff;
+    res->finite_backward = rep.fb;
+    res->finite_update = rep.fu;
+    res->max_abs_gradient = rep.max_g;
+    res->max_abs_update = rep.max_u;
+    res->numerics_probed = rep.probed;
+    res->numerics_reported = reported;
+    res->has_numerics_anomaly = anomaly;
+    res->recovery_action = TMNN_RECOVERY_NONE;
   }
 }
 
@@ -1552,6 +1685,25 @@ tmnn_status tmnn_cuda_train_step(tmnn_ctx *c, const float *positions,
   return guarded([&] {
     BusyGuard g(c);
     train_step(*c, positions, targets, n, flags, result);
+  });
+}
+
+tmnn_status tmnn_cuda_train_step_enqueue(tmnn_ctx *c, const float *positions,
+                                         const float *targets, uint32_t n,
+                                         uint32_t flags) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    train_step_enqueue(*c, positions, targets, n, flags);
+  });
+}
+
+tmnn_status tmnn_cuda_train_step_finalize(tmnn_ctx *c,
+                                          tmnn_step_result *result) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    BusyGuard g(c);
+    train_step_finalize(*c, result);
   });
 }
 

@@ -296,6 +296,7 @@ class Trainer:
         self.hash_count = plan["hash_grid_size"]
         self.mlp_count = plan["mlp_weight_count"]
         self.last_result = None
+        self._pending = []
 
     # ---------------------------------------------------------- creation
     @staticmethod
@@ -370,6 +371,35 @@ class Trainer:
         self._guarded(lambda: _check(
             lib.tmnn_cuda_train_step(h, pp, tp, n, flags, C.byref(res)),
             "training_step"))
+        self.last_result = res
+        return res.loss
+
+    def training_step_enqueue(self, input, target):
+        """Queue one training step without waiting for it (two may be in
+        flight; the upload of one overlaps the other's kernels).  The arrays
+        are kept alive, and must not be modified, until the step is
+        finalized.  Pair every call with training_step_finalize()."""
+        h = self._handle()
+        pp, n, f1, k1 = _arg(input, "input", self.n_input)
+        tp, nt, f2, k2 = _arg(target, "target", self.n_output)
+        if n != nt:
+            raise ValueError("input and target must have matching batch_size")
+        if f1 != f2:
+            raise ValueError("input and target must both be host or both CUDA")
+        self._guarded(lambda: _check(
+            lib.tmnn_cuda_train_step_enqueue(h, pp, tp, n, f1),
+            "training_step_enqueue"))
+        self._pending.append((k1, k2))
+
+    def training_step_finalize(self):
+        """Wait for the oldest enqueued step; returns its mean loss."""
+        h = self._handle()
+        res = _abi.StepResult()
+        self._guarded(lambda: _check(
+            lib.tmnn_cuda_train_step_finalize(h, C.byref(res)),
+            "training_step_finalize"))
+        if self._pending:
+            self._pending.pop(0)
         self.last_result = res
         return res.loss
 

@@ -122,6 +122,8 @@ _SIGS = [
     ("tmnn_cuda_set_initial_weights", C.c_int, [P, P, C.c_size_t, P, C.c_size_t]),
     ("tmnn_cuda_get_weights", C.c_int, [P, P, C.c_size_t, P, C.c_size_t]),
     ("tmnn_cuda_train_step", C.c_int, [P, P, P, u32, u32, C.POINTER(StepResult)]),
+    ("tmnn_cuda_train_step_enqueue", C.c_int, [P, P, P, u32, u32]),
+    ("tmnn_cuda_train_step_finalize", C.c_int, [P, C.POINTER(StepResult)]),
     ("tmnn_cuda_forward_backward", C.c_int,
      [P, P, P, u32, u32, C.POINTER(C.c_double)]),
     ("tmnn_cuda_read_buffer", C.c_int, [P, C.c_int32, P, C.c_size_t]),
