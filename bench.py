@@ -71,11 +71,17 @@ WORKLOADS = {
 # launch, --clock-control none), per workload and family; absent pairs report
 # traffic null.
 NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 187.64e6 / (1 << 18),
-                          ("field4d", "FullyFused"): 3753.30e6 / (1 << 18)}
+                          ("field4d", "FullyFused"): 3753.30e6 / (1 << 18),
+                          # Tiled: encode + MLP + scatter launches of one step
+                          ("sdf3d", "Tiled"): 171.66e6 / (1 << 18),
+                          ("field4d", "Tiled"): 1733.39e6 / (1 << 18)}
 # L2 side of the same captures: lts__t_bytes.sum per sample and
 # lts__throughput.avg.pct_of_peak_sustained_elapsed of that launch.
 NCU_L2 = {("sdf3d", "FullyFused"): (2373.08e6 / (1 << 18), 59.92),
-          ("field4d", "FullyFused"): (8279.80e6 / (1 << 18), 34.19)}
+          ("field4d", "FullyFused"): (8279.80e6 / (1 << 18), 34.19),
+          # Tiled: summed over its three launches, frac time-weighted
+          ("sdf3d", "Tiled"): (2843.19e6 / (1 << 18), 66.7),
+          ("field4d", "Tiled"): (7678.27e6 / (1 << 18), 59.9)}
 
 
 def log(*a):
