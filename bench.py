@@ -373,7 +373,7 @@ def dp_parity_check(t, tr, rank, world, local):
     def small(grad):
         w = dict(L=8, F=2, log2T=14, d=3, base=16.0, scale=1.447, W=64, H=1,
                  O=1, loss="L1", lr=1e-2, table="F16")
-        return t.Trainer.from_config(make_config(w, "FullyFused", grad, True),
+        return t.Trainer.from_config(make_config(w, "Auto", grad, True),
                                      n_input=3, n_output=1, device=local)
 
     def batches(steps, n):
@@ -390,7 +390,13 @@ def dp_parity_check(t, tr, rank, world, local):
         a = small(grad)
         uid = [t.dp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
+        # the replay's table is small (one bucket by default): split it so
+        # the bucketed exchange the benchmark uses is the one checked
+        saved = os.environ.get("TMNN_DP_BUCKETS")
+        os.environ["TMNN_DP_BUCKETS"] = saved or "2"
         a.dp_init(uid[0], rank, world)
+        if saved is None:
+            del os.environ["TMNN_DP_BUCKETS"]
         h0, m0 = a.weights()
         losses = []
         for pos, tgt in batches(steps, n * world):

@@ -112,6 +112,9 @@ def _gpu_rank(rank, world, port, q, family, grad, extra=None):
         sys.path.insert(0, p)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    # the test tables are small (one bucket by default): split them in four
+    # so the Tiled runs take the bucketed, pipelined exchange
+    os.environ["TMNN_DP_BUCKETS"] = "4"
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     import tmnn_b200 as t
