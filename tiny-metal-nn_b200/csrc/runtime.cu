@@ -2218,15 +2218,16 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
         if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
       for (auto &e : c->ev_adam)
         if (!e) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
-      // buckets of about 32 MiB of fp32 gradient, at most 8: smaller ones
-      // pay more in per-collective latency than their overlap wins
-      // (measured at 4 ranks: sdf3d, 64 MiB, 2 buckets 6442 steps/s, 4
-      // buckets 5189; field4d, 512 MiB, 4 buckets 1893, 1 bucket 1732)
+      // buckets of at least 32 MiB of fp32 gradient, at most 4: more,
+      // smaller ones pay more in per-collective latency and contention with
+      // the scatter than their overlap wins (measured at 4 ranks, steps/s:
+      // sdf3d, 64 MiB: 1 bucket 6312, 2 6618, 4 5189; field4d, 512 MiB:
+      // 1 bucket 1732, 4 1893, 8 1714, 16 1662)
       {
         const uint64_t mib = (c->hash_count * 4) >> 20;
         int g = (int)(mib / 32);
         if (g < 1) g = 1;
-        if (g > 8) g = 8;
+        if (g > 4) g = 4;
         c->dp_buckets = g;
       }
       if (const char *e = std::getenv("TMNN_DP_BUCKETS")) {
