@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -825,8 +826,10 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-template <int W, int NG>
-__global__ void __launch_bounds__(128 + 128 * NG)
+// S = 2 splits each tile's epilogue over two warpgroups (one half of the
+// columns each), halving the epilogue's share of the per-layer chain.
+template <int W, int NG, int S>
+__global__ void __launch_bounds__(128 + 128 * NG * S)
     k_mlp_pipe(const __grid_constant__ PipeParams P) {
   extern __shared__ __align__(128) uint8_t sm[];
   const NetDims &nd = P.nd;
@@ -841,7 +844,7 @@ __global__ void __launch_bounds__(128 + 128 * NG)
     for (uint32_t i = t; i < Ly.image_bytes / 16; i += blockDim.x) dst[i] = src[i];
     if (t < NG) {
       tc::mbar_init(tc::smem_u32(bars + t), 1);         // mma_done[g]
-      tc::mbar_init(tc::smem_u32(bars + NG + t), 128);  // act_ready[g]
+      tc::mbar_init(tc::smem_u32(bars + NG + t), 128 * S);  // act_ready[g]
     }
     if (warp == 0) tc::tmem_alloc(tc::smem_u32(tslot), P.tcols);
   }
@@ -903,34 +906,66 @@ __global__ void __launch_bounds__(128 + 128 * NG)
       }
     }
   } else if (warp >= 4) {
-    const int g = (warp - 4) >> 2;
-    const int r = t - 128 - 128 * g;  // row of the tile = TMEM lane
+    const int g = (warp - 4) / (4 * S);
+    const int part = ((warp - 4) >> 2) % S;  // column part of the epilogue
+    const int r = (t - 128) & 127;           // row of the tile = TMEM lane
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t acc = tmem + (uint32_t)g * P.gcols + lane_base;
     const uint32_t a_cols = acc + (uint32_t)W;
     const uint32_t done_bar = tc::smem_u32(bars + g);
     const uint32_t ready_bar = tc::smem_u32(bars + NG + g);
     uint32_t ph = 0;
+    // The input row of the group's next tile is loaded into registers while
+    // the current tile's layers run (parts of at most 64 columns: 8 x 16 B),
+    // so staging a tile does not wait on global memory.
+    const int cbeg = part * (In / S), cend = (part + 1) * (In / S);
+    constexpr int PB = (W / S) / 8 < 8 ? (W / S) / 8 : 8;  // 16-byte chunks
+    const bool pre = cend - cbeg <= 8 * PB;
+    uint4 nxt[PB];
+#define TMNN_FETCH_NEXT(TL)                                                   \
+  {                                                                           \
+    const uint32_t tl_ = (TL), rw_ = tl_ * kTile + r;                          \
+    const bool v_ = tl_ < P.ntiles && rw_ < P.N;                               \
+    const uint4 *src_ = reinterpret_cast<const uint4 *>(P.xin + (size_t)rw_ * In + cbeg); \
+    _Pragma("unroll") for (int j = 0; j < PB; ++j) {                          \
+      nxt[j] = make_uint4(0u, 0u, 0u, 0u);                                    \
+      if (v_ && cbeg + 8 * j < cend) nxt[j] = __ldg(src_ + j);                \
+    }                                                                         \
+  }
+    if (pre) TMNN_FETCH_NEXT(blockIdx.x * NG + g)
     for (uint32_t tile = blockIdx.x * NG + g; tile < P.ntiles && ok;
          tile += stride) {
       const uint32_t row = tile * kTile + r;
       const bool valid = row < P.N;
       // input row -> A columns (8 fp16 = 4 columns per 16-byte load)
-      for (int c0 = 0; c0 < In; c0 += 16) {
-        uint32_t u[8];
+      if (pre) {
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint4 x = make_uint4(0u, 0u, 0u, 0u);
-          if (valid)
-            x = __ldg(reinterpret_cast<const uint4 *>(P.xin + (size_t)row * In + c0) + q);
-          u[4 * q] = x.x;
-          u[4 * q + 1] = x.y;
-          u[4 * q + 2] = x.z;
-          u[4 * q + 3] = x.w;
+        for (int j = 0; j + 1 < PB; j += 2) {
+          if (cbeg + 8 * j >= cend) continue;  // uniform over the warp
+          const uint32_t u[8] = {nxt[j].x,     nxt[j].y,     nxt[j].z,
+                                 nxt[j].w,     nxt[j + 1].x, nxt[j + 1].y,
+                                 nxt[j + 1].z, nxt[j + 1].w};
+          tmem_st8(a_cols + (uint32_t)((cbeg + 8 * j) / 2), u);
         }
-        tmem_st8(a_cols + (uint32_t)(c0 / 2), u);
+      } else {
+        for (int c0 = cbeg; c0 < cend; c0 += 16) {
+          uint32_t u[8];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (valid)
+              x = __ldg(reinterpret_cast<const uint4 *>(P.xin + (size_t)row * In + c0) + q);
+            u[4 * q] = x.x;
+            u[4 * q + 1] = x.y;
+            u[4 * q + 2] = x.z;
+            u[4 * q + 3] = x.w;
+          }
+          tmem_st8(a_cols + (uint32_t)(c0 / 2), u);
+        }
       }
       tmem_st_wait();
+      if (pre) TMNN_FETCH_NEXT(tile + stride)
+#undef TMNN_FETCH_NEXT
       tc::fence_before_sync();
       mbar_arrive(ready_bar);
       for (int k = 0; k <= H && ok; ++k) {
@@ -943,9 +978,12 @@ __global__ void __launch_bounds__(128 + 128 * NG)
         tc::fence_after_sync();
         if (k < H) {
           const float4 *bk = reinterpret_cast<const float4 *>(sm + Ly.b[k]);
-          constexpr int CH = W < 64 ? W : 64;  // columns per TMEM load wait
+          constexpr int WP = W / S;               // this part's columns
+          constexpr int CHM = 32;  // register budget (the prefetched input row)
+          constexpr int CH = WP < CHM ? WP : CHM; // columns per TMEM load wait
 #pragma unroll
-          for (int c0 = 0; c0 < W; c0 += CH) {
+          for (int cc = 0; cc < WP; cc += CH) {
+            const int c0 = part * WP + cc;
             float v[CH];
             if (CH == 64)
               tc::tmem_ld64(acc + c0, v);
@@ -968,7 +1006,7 @@ __global__ void __launch_bounds__(128 + 128 * NG)
           tmem_st_wait();
           tc::fence_before_sync();
           mbar_arrive(ready_bar);
-        } else {
+        } else if (part == 0) {
           float y[kOutCols];
           tc::tmem_ld16(acc, y);
           tc::fence_before_sync();
@@ -1042,7 +1080,18 @@ int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
   P.err = ws.err;
   P.N = N;
   P.ntiles = (N + kTile - 1) / kTile;
-  const int NG = pipe_groups(nd);
+  // epilogue split over two warpgroups per tile (W = 128: 419 against 376
+  // TFLOP/s at H = 2, 578 against 543 at H = 4, N = 2^22; no gain at
+  // W <= 64), with at most three tiles in flight to stay within 1024
+  // threads; TMNN_PIPE_SPLIT=1 or 2 forces a choice (2 needs W >= 32 and
+  // In a multiple of 32)
+  // each part's input and hidden columns must be whole 16-column chunks
+  const bool can_split = nd.W >= 32 && nd.In % 32 == 0;
+  int split = nd.W >= 128 && can_split ? 2 : 1;  // measured: no gain at W <= 64
+  if (const char *e = std::getenv("TMNN_PIPE_SPLIT"))
+    split = (e[0] == '2' && can_split) ? 2 : 1;
+  int NG = pipe_groups(nd);
+  if (split == 2 && NG > 3) NG = 3;
   P.bar_off = align128(P.lay.image_bytes);
   P.gcols = pipe_gcols(nd);
   P.tcols = 32;
@@ -1051,11 +1100,14 @@ int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
   const uint32_t smem = pipe_smem(nd);
   using PipeFn = void (*)(PipeParams);
   PipeFn fn = nullptr;
-#define TMNN_PIPE(WW)                                      \
-  case WW:                                                 \
-    fn = NG == 2 ? k_mlp_pipe<WW, 2>                       \
-         : NG == 3 ? k_mlp_pipe<WW, 3> : NG == 4 ? k_mlp_pipe<WW, 4> \
-         : NG == 5 ? k_mlp_pipe<WW, 5> : k_mlp_pipe<WW, 6>; \
+#define TMNN_PIPE(WW)                                                       \
+  case WW:                                                                  \
+    if (split == 2)                                                         \
+      fn = NG == 2 ? k_mlp_pipe<WW, 2, 2> : k_mlp_pipe<WW, 3, 2>;           \
+    else                                                                    \
+      fn = NG == 2 ? k_mlp_pipe<WW, 2, 1>                                   \
+           : NG == 3 ? k_mlp_pipe<WW, 3, 1> : NG == 4 ? k_mlp_pipe<WW, 4, 1> \
+           : NG == 5 ? k_mlp_pipe<WW, 5, 1> : k_mlp_pipe<WW, 6, 1>;         \
     break;
   switch (nd.W) { TMNN_PIPE(16) TMNN_PIPE(32) TMNN_PIPE(64) TMNN_PIPE(128) }
 #undef TMNN_PIPE
@@ -1065,7 +1117,7 @@ int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
   uint32_t grid = (P.ntiles + NG - 1) / NG;
   if (grid > (uint32_t)num_sms) grid = (uint32_t)num_sms;
   if (grid == 0) return launches;
-  fn<<<grid, 128 + 128 * NG, smem, st>>>(P);
+  fn<<<grid, 128 + 128 * NG * split, smem, st>>>(P);
   return launches + 1;
 }
 
