@@ -111,3 +111,16 @@ def test_valid_config_fails_cleanly_without_gpu():
     st, msg, h = _create('{"loss": {"otype": "L1"}, "optimizer": {"learning_rate": 0.01}}')
     assert st != 0 and "device" in msg.lower()
     assert not h.value
+
+
+def test_reference_import_name():
+    """`import tiny_metal_nn` gives the same front end as tmnn_b200, with the
+    reference's Trainer methods (is_gpu_available included)."""
+    import tiny_metal_nn
+    import tmnn_b200
+    assert tiny_metal_nn.Trainer is tmnn_b200.Trainer
+    assert issubclass(tiny_metal_nn.ConfigError, ValueError)
+    assert issubclass(tiny_metal_nn.DTypeError, TypeError)
+    for name in ("from_config", "training_step", "inference", "step",
+                 "close", "is_gpu_available"):
+        assert hasattr(tiny_metal_nn.Trainer, name)

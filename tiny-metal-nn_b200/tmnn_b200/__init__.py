@@ -551,6 +551,12 @@ class Trainer:
         return feat, idx, cells
 
     # ---------------------------------------------------------- state
+    def is_gpu_available(self):
+        """True while the trainer holds its CUDA device (the reference's
+        Trainer.is_gpu_available, src/python/tmnn_pybind.cpp:337-342)."""
+        self._handle()
+        return True
+
     def step(self):
         s = C.c_uint32()
         _check(lib.tmnn_cuda_get_step(self._handle(), C.byref(s)))
