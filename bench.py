@@ -543,7 +543,8 @@ def nerf_cpu_baseline(w, seconds=12.0):
 def run_nerf(args, w, rank, world, local, emit):
     """NeRF-style field: one step = density forward,
     colour network train, density backward + scatter, Adam on both, over
-    2^20 samples per GPU (data parallel only as independent replicas)."""
+    2^20 samples per GPU, data parallel over the ranks (colour gradients
+    and losses summed by allreduce, density gradients by its exchange)."""
     import torch
     import tmnn_b200 as t
     torch.cuda.set_device(local)
@@ -551,6 +552,11 @@ def run_nerf(args, w, rank, world, local, emit):
                      log2_hashmap_size=w["log2T"], base_resolution=w["base"],
                      per_level_scale=w["scale"], lr=w["lr"],
                      family=args.family, table_dtype=w["table"], device=local)
+    if world > 1:
+        import torch.distributed as dist
+        uid = [t.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        nf.dp_init(uid[0], rank, world)
     B = w["batch"]
     pool = [[torch.from_numpy(a).cuda() for a in nerf_batch_np(B, 1000 * rank + i)]
             for i in range(2)]
@@ -624,7 +630,7 @@ def run_nerf(args, w, rank, world, local, emit):
         "dtype": "f32 table / f16 tensor-core MLPs, f32 accumulate",
         "data": "synthetic",
         "config": {"workload": "nerf", "desc": w["desc"], "batch_per_gpu": B,
-                   "global_batch": B * world, "parallelism": f"replicas{world}",
+                   "global_batch": B * world, "parallelism": f"dp{world}",
                    "l2": "no flush: per-step working set (fp32 table, m, v, "
                          "gradients, 2^20-sample buffers) exceeds the 126 MB L2"},
         "samples_per_s": value * B, "inference_samples_per_s": inf_sps,

@@ -378,6 +378,13 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *nerf, const float *positions,
                                       const float *directions,
                                       const float *rgb, const float *sigma,
                                       uint32_t n, uint32_t flags, float *loss);
+/* Data-parallel training of the field (no reference counterpart): the same
+ * unique id / rank / world as tmnn_cuda_dp_init.  Each rank trains on its
+ * shard of every batch; the colour network's gradients and the losses are
+ * summed over the ranks before its Adam step, the density network exchanges
+ * its own gradients, and all means are over the global batch. */
+tmnn_status tmnn_cuda_nerf_dp_init(tmnn_nerf *nerf, const uint8_t unique_id[128],
+                                   int rank, int world);
 /* rgb [n x 3] (after the sigmoid) and sigma [n] (after exp). */
 tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *nerf, const float *positions,
                                      const float *directions, float *rgb,

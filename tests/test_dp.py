@@ -271,3 +271,78 @@ def test_dp_sharded_safe_family_retry_matches_one_process():
         return a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300)
     assert cos(h0 - hi, hr - hi) >= 0.999
     assert cos(m0 - mi, mr - mi) >= 0.999
+
+
+NERF_KW = dict(n_levels=8, n_features_per_level=2, log2_hashmap_size=14,
+               base_resolution=16.0, per_level_scale=1.382)
+
+
+def _nerf_rank(rank, world, port, q):
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),
+              os.path.join(ROOT, "oracle")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import oracle as o
+    import tmnn_b200 as t
+    nf = t.NerfField(family="FullyFused", device=rank, **NERF_KW)
+    uid = [t.dp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    nf.dp_init(uid[0], rank, world)
+    c0 = nf.color_weights()
+    losses = []
+    for s in range(3):
+        pos, d, rgb, sig = o.nerf_batch(4096, 40 + s)
+        n = pos.shape[0] // world
+        sl = slice(rank * n, (rank + 1) * n)
+        losses.append(nf.training_step(*(np.ascontiguousarray(a[sl])
+                                          for a in (pos, d, rgb, sig))))
+    nf.density.dp_sync_state()
+    q.put((rank, losses, c0, nf.color_weights(), nf.density.weights()))
+    nf.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_dp_nerf_two_gpus_match_one():
+    """The NeRF field trained data parallel (each rank a slice of every
+    batch) against one process on the whole batch: losses within 1e-3,
+    colour and density weight changes aligned."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import oracle as o
+    import tmnn_b200 as t
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_nerf_rank, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, losses, c0, c1, dw = q.get(timeout=120)
+        res[r] = (losses, c0, c1, dw)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = t.NerfField(family="FullyFused", **NERF_KW)
+    h0, m0 = ref.density.weights()
+    lr = [ref.training_step(*o.nerf_batch(4096, 40 + s)) for s in range(3)]
+    cr = ref.color_weights()
+    hr, mr = ref.density.weights()
+    ref.close()
+    (l0, c0, c1, (h1, m1)), (_, _, c1b, (h1b, m1b)) = res[0], res[1]
+    assert np.array_equal(c1, c1b) and np.array_equal(h1, h1b)
+    assert np.allclose(l0, lr, rtol=1e-3)
+
+    def cos(a, b):
+        a, b = a.astype(np.float64), b.astype(np.float64)
+        return a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300)
+    assert cos(c1 - c0, cr - c0) >= 0.999
+    assert cos(h1 - h0, hr - h0) >= 0.999
+    assert cos(m1 - m0, mr - m0) >= 0.999

@@ -24,6 +24,7 @@
 #include "../../include/tmnn_cuda.h"
 #include "fused.h"
 #include "kernels.h"
+#include "runtime.h"
 
 using namespace tmnn;
 
@@ -341,7 +342,9 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *n, const float *pos,
     const float *d = stage(*n, dirs, (size_t)N * 3, n->dirs_d, flags);
     const float *c = stage(*n, rgb, (size_t)N * 3, n->rgb_d, flags);
     const float *s = stage(*n, sigma, N, n->sig_d, flags);
-    const float inv_N = 1.0f / (float)N;
+    // data parallel: every mean is over the global batch (equal shards)
+    const uint64_t global_n = (uint64_t)N * (uint64_t)ctx_world(n->density);
+    const float inv_N = 1.0f / (float)global_n;
     const bool prof = flags & TMNN_PROFILE;
     if (prof) CKN(cudaEventRecord(n->ev[0], n->stream));
     front(*n, p, d, N);
@@ -355,6 +358,9 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *n, const float *pos,
     k_nerf_dens_grad<<<(N + 255) / 256, 256, 0, n->stream>>>(
         n->dens.p, s, n->dx.p, inv_N, n->dy.p, n->loss.p + 1, N);
     n->launches++;
+    // colour gradients and both losses summed over the ranks (the density
+    // network's gradients are exchanged by its own adam_step)
+    ctx_allreduce_sum(n->density, n->cg.p, n->cnd.mlp_count, n->loss.p, 2);
     colour_adam(*n);
     CKN(cudaMemcpyAsync(n->h_loss, n->loss.p, 2 * sizeof(double),
                         cudaMemcpyDeviceToHost, n->stream));
@@ -374,8 +380,14 @@ tmnn_status tmnn_cuda_nerf_train_step(tmnn_nerf *n, const float *pos,
     if (fused_error(n->ws, n->stream))
       throw std::runtime_error("nerf: colour kernel pipeline wait timed out");
     if (loss)
-      *loss = (float)((n->h_loss[0] + n->h_loss[1]) / (double)N);
+      *loss = (float)((n->h_loss[0] + n->h_loss[1]) / (double)global_n);
   });
+}
+
+tmnn_status tmnn_cuda_nerf_dp_init(tmnn_nerf *n, const uint8_t unique_id[128],
+                                   int rank, int world) {
+  if (!n) return TMNN_ERR_NULL_OBJECT;
+  return tmnn_cuda_dp_init(n->density, unique_id, rank, world);
 }
 
 tmnn_status tmnn_cuda_nerf_inference(tmnn_nerf *n, const float *pos,

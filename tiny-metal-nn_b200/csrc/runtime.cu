@@ -1549,6 +1549,20 @@ void backward_accumulate(tmnn_ctx &c, const float *pos, const float *dout,
 
 // ====================================================================== ABI
 
+namespace tmnn {
+int ctx_world(const tmnn_ctx *c) { return c ? c->world : 1; }
+void ctx_allreduce_sum(tmnn_ctx *c, float *f32, size_t n32, double *f64,
+                       size_t n64) {
+  if (!c || !c->comm || c->world <= 1) return;
+  NK(ncclGroupStart());
+  if (n32)
+    NK(ncclAllReduce(f32, f32, n32, ncclFloat32, ncclSum, c->comm, c->stream));
+  if (n64)
+    NK(ncclAllReduce(f64, f64, n64, ncclFloat64, ncclSum, c->comm, c->stream));
+  NK(ncclGroupEnd());
+}
+}  // namespace tmnn
+
 extern "C" {
 
 void tmnn_cuda_default_train_cfg(tmnn_train_cfg *c) {

@@ -13,6 +13,13 @@ namespace tmnn {
 void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
                       tmnn_spec *spec, tmnn_train_cfg *cfg);
 
+// Data-parallel helpers for objects built on a context (nerf.cu): the
+// context's rank count, and an in-place sum over its ranks on its stream
+// (no-op with one rank).
+int ctx_world(const tmnn_ctx *c);
+void ctx_allreduce_sum(tmnn_ctx *c, float *f32, size_t n32, double *f64,
+                       size_t n64);
+
 // tmnn::PlannerFallbackReason values
 // (include/tiny-metal-nn/detail/network_planning.h:45-59).
 enum PlannerFallbackReason : int32_t {

@@ -256,6 +256,13 @@ class NerfField:
     def stream(self):
         return self.density.stream()
 
+    def dp_init(self, unique_id: bytes, rank: int, world: int):
+        """Data-parallel training over `world` ranks (one per GPU): each rank
+        passes its shard of every batch; gradients and losses are summed
+        over the ranks."""
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        _check_nerf(lib.tmnn_cuda_nerf_dp_init(self._h, buf, rank, world))
+
     def close(self):
         if self._h is not None:
             self.density.close()

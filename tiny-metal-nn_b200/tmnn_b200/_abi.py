@@ -160,6 +160,7 @@ _SIGS = [
     ("tmnn_cuda_nerf_create", C.c_int, [C.c_int, C.POINTER(NerfCfg), C.POINTER(P)]),
     ("tmnn_cuda_nerf_destroy", C.c_int, [P]),
     ("tmnn_cuda_nerf_density", C.c_int, [P, C.POINTER(P)]),
+    ("tmnn_cuda_nerf_dp_init", C.c_int, [P, P, C.c_int, C.c_int]),
     ("tmnn_cuda_nerf_color_weights", C.c_int, [P, P, P, C.c_size_t]),
     ("tmnn_cuda_nerf_train_step", C.c_int,
      [P, P, P, P, P, u32, u32, C.POINTER(C.c_float)]),
