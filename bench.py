@@ -907,8 +907,13 @@ def main():
         # the pipelined public API: while step i runs, the host->device copy
         # of step i+1 (pinned memory, copy stream) is already queued; every
         # step's loss is read back by its finalize
-        for i in range(3):
-            tr.training_step(*hpool[i % 4])
+        # warm-up through the same API: the first enqueue of each lane
+        # allocates its device copy of the batch and its pinned statistics
+        for i in range(4):
+            tr.training_step_enqueue(*hpool[i % 4])
+            if i:
+                tr.training_step_finalize()
+        tr.training_step_finalize()
         barrier(world)
         torch.cuda.synchronize()
         t_wall = time.perf_counter()
