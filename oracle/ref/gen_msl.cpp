@@ -3,8 +3,10 @@
 // kernel text for one spec.  Test infrastructure: its output is compiled as
 // C++ by oracle/ref_build.py through oracle/ref/metal_shim.h.
 //
-// usage: gen_msl ROLE L F log2T d W H O loss base scale huber active_mask
+// usage: gen_msl ROLE L F log2T d W H O loss base scale huber active_mask [simd]
 //   ROLE: train | eval | fwd | extgrad | evalgrad
+//   simd: 1 lets the compiler realise the simdgroup-matrix training kernel
+//   (the reference's default for the shapes that allow it); default 0.
 #include "tiny-metal-nn/kernels/kernel_compiler.h"
 #include <cstdio>
 #include <cstdlib>
@@ -29,7 +31,7 @@ int main(int argc, char **argv) {
   s.emit_active_hash_mask = std::atoi(argv[13]) != 0;
   auto schema = tmnn::KernelCompiler::makeDefaultSchema(s);
   tmnn::extension::KernelCompileSpec cs;
-  cs.allow_simd = false;
+  cs.allow_simd = argc > 14 && std::atoi(argv[14]) != 0;
   cs.allow_fp16 = false;
   cs.allow_tg_weight_cache = false;
   cs.loss_kind = static_cast<tmnn::extension::LossKind>(std::atoi(argv[9]));

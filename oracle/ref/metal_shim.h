@@ -8,7 +8,9 @@
 // Semantics: vectors are plain value types with component-wise operators;
 // address-space qualifiers vanish; atomics map to std::atomic; a threadgroup
 // is emulated by running its threads as std::threads that meet at a
-// std::barrier (the driver sets the current barrier per thread).
+// std::barrier (the driver sets the current barrier per thread); the
+// simdgroup operations of the SIMD training kernel are emulated per lane
+// (below).
 #pragma once
 #include <atomic>
 #include <barrier>
@@ -94,6 +96,11 @@ inline float clamp(float x, float lo, float hi) { return min(max(x, lo), hi); }
 inline bool isnan(float x) { return std::isnan(x); }
 inline bool isinf(float x) { return std::isinf(x); }
 inline bool isfinite(float x) { return std::isfinite(x); }
+inline float2 floor(float2 v) { return float2(floor(v.x), floor(v.y)); }
+inline float3 floor(float3 v) { return float3(floor(v.x), floor(v.y), floor(v.z)); }
+inline float4 floor(float4 v) {
+  return float4(floor(v.x), floor(v.y), floor(v.z), floor(v.w));
+}
 inline float4 max(float4 a, float4 b) {
   return float4(max(a.x, b.x), max(a.y, b.y), max(a.z, b.z), max(a.w, b.w));
 }
@@ -128,6 +135,94 @@ enum class mem_flags { mem_none, mem_device, mem_threadgroup };
 extern thread_local std::barrier<> *g_tg_barrier;
 inline void threadgroup_barrier(mem_flags) {
   if (g_tg_barrier) g_tg_barrier->arrive_and_wait();
+}
+
+// ---- simdgroup operations (the reference's SIMD training kernel) ----------
+// A simdgroup is 32 consecutive threads of the emulated threadgroup, which
+// meet at their own std::barrier (set per thread by the driver, with the
+// lane index and 32 floats of per-simdgroup scratch).  MSL executes these
+// operations collectively; here every lane holds a full copy of each 8x8
+// matrix (all lanes load the same elements), computes the product itself,
+// and one lane writes results back, with a simdgroup barrier before every
+// collective load, sum and store so the lanes' earlier writes are visible.
+// The summation order inside a product is row-by-column in k order, so
+// results agree with the hardware's to rounding, not bit for bit.
+extern thread_local std::barrier<> *g_simd_barrier;
+extern thread_local unsigned g_simd_lane;
+extern thread_local float *g_simd_scratch;
+inline void simd_sync() {
+  if (g_simd_barrier) g_simd_barrier->arrive_and_wait();
+}
+
+typedef V2<unsigned long> ulong2;
+
+template <class T> struct simdgroup_matrix8 {
+  T e[8][8];
+};
+typedef simdgroup_matrix8<float> simdgroup_float8x8;
+typedef simdgroup_matrix8<half> simdgroup_half8x8;
+
+// m(r, c) = src[(origin.y + r) * elements_per_row + origin.x + c], or with
+// transpose the element at (c, r) of the source block.
+template <class T, class S>
+inline void simdgroup_load(simdgroup_matrix8<T> &m, const S *src,
+                           unsigned long elements_per_row,
+                           ulong2 origin = ulong2(0ul, 0ul),
+                           bool transpose = false) {
+  simd_sync();
+  for (int r = 0; r < 8; ++r)
+    for (int c = 0; c < 8; ++c) {
+      const unsigned long rr = transpose ? c : r, cc = transpose ? r : c;
+      m.e[r][c] = T(src[(origin.y + rr) * elements_per_row + origin.x + cc]);
+    }
+}
+
+template <class T, class D>
+inline void simdgroup_store(const simdgroup_matrix8<T> &m, D *dst,
+                            unsigned long elements_per_row,
+                            ulong2 origin = ulong2(0ul, 0ul),
+                            bool transpose = false) {
+  simd_sync();
+  if (g_simd_lane == 0)
+    for (int r = 0; r < 8; ++r)
+      for (int c = 0; c < 8; ++c) {
+        const unsigned long rr = transpose ? c : r, cc = transpose ? r : c;
+        dst[(origin.y + rr) * elements_per_row + origin.x + cc] = D(m.e[r][c]);
+      }
+  simd_sync();
+}
+
+template <class T>
+inline void simdgroup_multiply_accumulate(simdgroup_matrix8<T> &d,
+                                          const simdgroup_matrix8<T> &a,
+                                          const simdgroup_matrix8<T> &b,
+                                          const simdgroup_matrix8<T> &c) {
+  simdgroup_matrix8<T> out;
+  for (int i = 0; i < 8; ++i)
+    for (int j = 0; j < 8; ++j) {
+      T acc = c.e[i][j];
+      for (int k = 0; k < 8; ++k) acc = acc + a.e[i][k] * b.e[k][j];
+      out.e[i][j] = acc;
+    }
+  d = out;
+}
+
+template <class T>
+inline void simdgroup_multiply(simdgroup_matrix8<T> &d,
+                               const simdgroup_matrix8<T> &a,
+                               const simdgroup_matrix8<T> &b) {
+  simdgroup_matrix8<T> z{};
+  simdgroup_multiply_accumulate(d, a, b, z);
+}
+
+// Sum over the 32 lanes of the simdgroup, in lane order.
+inline float simd_sum(float x) {
+  g_simd_scratch[g_simd_lane] = x;
+  simd_sync();
+  float s = 0.0f;
+  for (int l = 0; l < 32; ++l) s = s + g_simd_scratch[l];
+  simd_sync();
+  return s;
 }
 
 }  // namespace metal

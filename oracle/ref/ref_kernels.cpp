@@ -28,6 +28,26 @@ void tmnn_ref_train(const float *pos, const float *tgt, const float *cfg,
           lid);
     });
 }
+#elif defined(ROLE_TRAIN_SIMD)
+// neural_sdf_train_forward_backward, simdgroup-matrix variant: threadgroups
+// of SIMD_TG_SIZE threads over TOTAL_PTS_PER_TG points (batches of
+// POINTS_PER_TG rows)
+void tmnn_ref_train_simd(const float *pos, const float *tgt, const float *cfg,
+                         const float *hash, int32_t *grad_hash, float *grad_mlp,
+                         float *loss_partials, const float *train_params,
+                         uint32_t *mask, uint32_t *summary, const float *mlp,
+                         uint32_t N) {
+  const uint32_t tgs = (N + TOTAL_PTS_PER_TG - 1) / TOTAL_PTS_PER_TG;
+  for (uint32_t tg = 0; tg < tgs; ++tg)
+    run_threadgroup(SIMD_TG_SIZE, [&](unsigned lid) {
+      ref_k::neural_sdf_train_forward_backward(
+          pos, tgt, cfg, hash, reinterpret_cast<atomic_int *>(grad_hash),
+          reinterpret_cast<atomic_float *>(grad_mlp), loss_partials,
+          train_params, reinterpret_cast<atomic_uint *>(mask),
+          reinterpret_cast<atomic_uint *>(summary), mlp, tg, lid);
+    });
+}
+uint32_t tmnn_ref_train_simd_points_per_tg() { return TOTAL_PTS_PER_TG; }
 #elif defined(ROLE_EXTGRAD)
 void tmnn_ref_extgrad(const float *pos, const float *tgt, const float *cfg,
                       const float *hash, int32_t *grad_hash, float *grad_mlp,

@@ -7,8 +7,10 @@ copied into this repository):
   _ref/gen_msl                 the reference's KernelCompiler/MLPKernelEmitter
   _ref/libtmnn_ref_host.so     morton_sort.h, kernel_spec.cpp, adam_params.h
   _ref/libtmnn_ref_<tag>.so    the scalar train / external-grad / eval MSL the
-                               emitter generates for spec <tag>, compiled as
-                               C++ through oracle/ref/metal_shim.h
+                               emitter generates for spec <tag> (and its
+                               simdgroup-matrix train kernel where the
+                               compiler realises one), compiled as C++
+                               through oracle/ref/metal_shim.h
   _ref/libtmnn_ref_static.so   the static Adam MSL (adam_kernel_msl.h) and the
                                Philox init MSL (metal_context.cpp)
 
@@ -69,6 +71,24 @@ def float_literals(msl):
     return re.sub(r"(?<![\w.])(\d+\.\d*)(?![\w.])", r"\1f", msl)
 
 
+def threadgroup_qualifiers(msl):
+    """The shim maps `threadgroup` to `static`, which is right for the
+    arrays a kernel body declares (one threadgroup runs at a time) but not
+    for threadgroup pointers or array parameters (the SIMD training kernel
+    passes its activation tiles to helpers): there the qualifier is dropped."""
+    out, i = [], 0
+    for m in re.finditer(r"\bthreadgroup\b(?!_)", msl):
+        rest = msl[m.end():]
+        stop = re.search(r"[;,)]", rest)
+        stmt = rest[:stop.start()] if stop else rest
+        body_array = stop and stop.group() == ";" and "=" not in stmt and "[" in stmt
+        out.append(msl[i:m.start()])
+        out.append("threadgroup" if body_array else "")
+        i = m.end()
+    out.append(msl[i:])
+    return "".join(out)
+
+
 def run(cmd, **kw):
     subprocess.run(cmd, check=True, **kw)
 
@@ -116,13 +136,22 @@ def build(force=False):
                  ("eval", "ROLE_EVAL")]
         if sp[6] == 1:  # the EvalGradient kernel is single-output
             roles.append(("evalgrad", "ROLE_EVALGRAD"))
+        # the simdgroup-matrix training kernel, for the shapes where the
+        # reference's compiler realises it (its default there)
+        probe = subprocess.run([gen, "train"] + args + ["1", "1"], check=True,
+                               capture_output=True, text=True)
+        if "simd=1" in probe.stderr:
+            roles.append(("train_simd", "ROLE_TRAIN_SIMD"))
         for role, define in roles:
             msl = os.path.join(OUT, f"{tag}_{role}.msl")
-            text = subprocess.run(
-                [gen, role] + args + ["0" if role.startswith("eval") else "1"],
-                check=True, capture_output=True, text=True).stdout
+            gen_role = "train" if role == "train_simd" else role
+            flags = ["0" if role.startswith("eval") else "1"]
+            if role == "train_simd":
+                flags.append("1")
+            text = subprocess.run([gen, gen_role] + args + flags, check=True,
+                                  capture_output=True, text=True).stdout
             with open(msl, "w") as f:
-                f.write(float_literals(text))
+                f.write(threadgroup_qualifiers(float_literals(text)))
             obj = os.path.join(OUT, f"{tag}_{role}.o")
             run(CXX + shim + ["-c", drv, f"-D{define}",
                               f'-DMSL_FILE="{msl}"', "-o", obj])

@@ -82,6 +82,42 @@ def train(tag, sp, table, mlp, pos, tgt, d_out=None, active_levels=0):
                 summary=summ)
 
 
+def has_simd_train(tag):
+    """Whether the reference's compiler realises the simdgroup-matrix
+    training kernel for spec `tag` (then its default training kernel)."""
+    return available(tag) and hasattr(_lib(tag), "tmnn_ref_train_simd")
+
+
+def train_simd(tag, sp, table, mlp, pos, tgt, active_levels=0):
+    """Runs the reference's simdgroup-matrix train kernel (threadgroups of
+    32 threads over 64 points, 8-row simdgroup tiles).  Same outputs as
+    train()."""
+    L, F, log2T, d, W, H, O = sp[:7]
+    lib = _lib(tag)
+    pos = np.ascontiguousarray(pos, np.float32)
+    N = pos.shape[0]
+    tgt = np.ascontiguousarray(tgt, np.float32)
+    cfg = _config(L, F, log2T, sp[8], sp[9], W, H, N, mlp)
+    gh = np.zeros(table.size, np.int32)
+    gm = np.zeros(mlp.size, np.float32)
+    lib.tmnn_ref_train_simd_points_per_tg.restype = C.c_uint32
+    per = lib.tmnn_ref_train_simd_points_per_tg()
+    tgs = (N + per - 1) // per
+    lp = np.zeros(max(tgs, 1), np.float32)
+    tp = np.array([N, 0, 1.0, active_levels if active_levels > 0 else L, 0, 0,
+                   0, 0], np.float32)
+    slots = table.size // 2 if F == 2 else table.size
+    mask = np.zeros((slots + 31) // 32, np.uint32)
+    summ = np.zeros((slots + 2047) // 2048 + 1, np.uint32)
+    table = np.ascontiguousarray(table, np.float32)
+    mlp = np.ascontiguousarray(mlp, np.float32)
+    lib.tmnn_ref_train_simd(_p(pos), _p(tgt), _p(cfg), _p(table), _p(gh),
+                            _p(gm), _p(lp), _p(tp), _p(mask), _p(summ),
+                            _p(mlp), C.c_uint32(N))
+    return dict(loss_partials=lp, grad_hash=gh, grad_mlp=gm, mask=mask,
+                summary=summ)
+
+
 def mask_to_touched(mask, slots):
     bits = np.unpackbits(mask.view(np.uint8), bitorder="little")
     return bits[:slots].astype(np.uint8)

@@ -5,7 +5,7 @@ reference's generated MSL kernels and host code compiled here).
 The fixtures let the parity tests pin the oracle and the CUDA path on machines
 where the reference sources are absent.  Inputs are regenerated from the
 seeds below (numpy PCG64), so each fixture stores only the reference's
-outputs.  Run: python tests/golden/make_golden.py
+outputs.  Run: python tests/golden/make_golden.py [simd]
 """
 from __future__ import annotations
 
@@ -22,6 +22,9 @@ import ref_oracle  # noqa: E402
 
 N_POINTS = 300
 TAGS = ("ka", "sdf", "img", "d4", "f1", "f4", "cos")
+# specs for which the reference's compiler realises the simdgroup-matrix
+# training kernel (one output, one or two hidden layers)
+SIMD_TAGS = ("sdf", "f4")
 # single-output specs whose EvalGradient kernel output is also stored
 EVALGRAD_ONLY = ("d4o1", "h3")
 
@@ -41,7 +44,23 @@ def case_inputs(tag, sp, seed=1):
     return table, mlp, pos, tgt, d_out
 
 
+def simd_main():
+    """ref_simd_<tag>.npz: the simdgroup-matrix training kernel (the
+    reference's default for these shapes) on the same inputs as ref_<tag>."""
+    for tag in SIMD_TAGS:
+        sp = ref_oracle.spec_tuple(tag)
+        table, mlp, pos, tgt, _ = case_inputs(tag, sp)
+        tr = ref_oracle.train_simd(tag, sp, table, mlp, pos, tgt)
+        nz = np.nonzero(tr["grad_hash"])[0].astype(np.uint32)
+        np.savez_compressed(
+            os.path.join(HERE, f"ref_simd_{tag}.npz"),
+            spec=np.array(sp, np.float64), hash_idx=nz,
+            hash_val=tr["grad_hash"][nz], mlp=tr["grad_mlp"],
+            loss_sum=np.float64(tr["loss_partials"].sum()), mask=tr["mask"])
+
+
 def main():
+    simd_main()
     for tag in TAGS:
         sp = ref_oracle.spec_tuple(tag)
         table, mlp, pos, tgt, d_out = case_inputs(tag, sp)
@@ -101,4 +120,5 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    # "simd": write only the SIMD-kernel fixtures
+    simd_main() if sys.argv[1:] == ["simd"] else main()
