@@ -74,14 +74,19 @@ NCU_TRAFFIC_PER_SAMPLE = {("sdf3d", "FullyFused"): 187.64e6 / (1 << 18),
                           ("field4d", "FullyFused"): 3753.30e6 / (1 << 18),
                           # Tiled: encode + MLP + scatter launches of one step
                           ("sdf3d", "Tiled"): 171.66e6 / (1 << 18),
-                          ("field4d", "Tiled"): 1733.39e6 / (1 << 18)}
+                          ("field4d", "Tiled"): 1733.39e6 / (1 << 18),
+                          # fp16 hash gradients (workload + "_grad_f16")
+                          ("sdf3d_grad_f16", "Tiled"): 125.26e6 / (1 << 18),
+                          ("field4d_grad_f16", "Tiled"): 800.51e6 / (1 << 18)}
 # L2 side of the same captures: lts__t_bytes.sum per sample and
 # lts__throughput.avg.pct_of_peak_sustained_elapsed of that launch.
 NCU_L2 = {("sdf3d", "FullyFused"): (2373.08e6 / (1 << 18), 59.92),
           ("field4d", "FullyFused"): (8279.80e6 / (1 << 18), 34.19),
           # Tiled: summed over its three launches, frac time-weighted
           ("sdf3d", "Tiled"): (2843.19e6 / (1 << 18), 66.7),
-          ("field4d", "Tiled"): (7678.27e6 / (1 << 18), 59.9)}
+          ("field4d", "Tiled"): (7678.27e6 / (1 << 18), 59.9),
+          ("sdf3d_grad_f16", "Tiled"): (2763.29e6 / (1 << 18), 66.2),
+          ("field4d_grad_f16", "Tiled"): (6891.47e6 / (1 << 18), 71.2)}
 
 
 def log(*a):
@@ -233,13 +238,13 @@ def hbm_peak():
 
 
 def time_training(t, name, args, rank, world, local, steps, warmup,
-                  phase_steps, clocks=False):
+                  phase_steps, clocks=False, grad=None):
     """Trains workload w for `warmup` untimed and `steps` timed steps with
     device-resident inputs (CUDA events on the library's stream, max over
     ranks), then `phase_steps` profiled steps for the per-phase split."""
     import torch
     w = WORKLOADS[name]
-    tr = t.Trainer.from_config(make_config(w, args.family, args.grad,
+    tr = t.Trainer.from_config(make_config(w, args.family, grad or args.grad,
                                            not args.no_morton,
                                            args.morton_bits),
                                n_input=w["d"], n_output=w["O"], device=local)
@@ -291,11 +296,13 @@ def time_training(t, name, args, rank, world, local, steps, warmup,
     # algorithmic bytes per sample of the forward/backward: every corner's
     # table entry gathered once and its gradient reduced once, plus the
     # point's position and target
-    per_sample = w["L"] * nc * w["F"] * (tbytes + 4) + (w["d"] + w["O"]) * 4
+    gbytes = 2 if (grad or args.grad) == "F16" else 4
+    per_sample = w["L"] * nc * w["F"] * (tbytes + gbytes) + (w["d"] + w["O"]) * 4
     fb_ms = statistics.mean(fb)
     achieved = per_sample * B / (fb_ms / 1000.0) / 1e9
-    traffic = NCU_TRAFFIC_PER_SAMPLE.get((name, plan["family"]))
-    l2 = NCU_L2.get((name, plan["family"]))
+    fmt = "" if gbytes == 4 else "_grad_f16"
+    traffic = NCU_TRAFFIC_PER_SAMPLE.get((name + fmt, plan["family"]))
+    l2 = NCU_L2.get((name + fmt, plan["family"]))
     return {
         "trainer": tr, "plan": plan, "pool": pool, "stream": stream,
         "family": plan["family"],
@@ -322,11 +329,12 @@ def time_training(t, name, args, rank, world, local, steps, warmup,
     }
 
 
-def adam_traffic_bytes(tr, batch, w):
+def adam_traffic_bytes(tr, batch, w, grad):
     """Algorithmic bytes of one sparse Adam launch for a batch like `batch`:
-    the kernel reads every hash gradient (4 B) and the touched map, and for
-    each group of four parameters holding a touched slot reads and writes w,
-    m, v (24 B each), clears the gradient (4 B) and, with an fp16 table,
+    the kernel reads every hash gradient (4 B, fp16 gradients 2 B) and the
+    touched map, and for each group of four parameters holding a touched
+    slot reads and writes w, m, v (24 B each), clears the gradient and, with
+    an fp16 table,
     writes the gather copy (2 B); the MLP is updated densely (28 B each)."""
     tr.zero_gradients()
     tr.forward_backward(*batch)
@@ -338,7 +346,8 @@ def adam_traffic_bytes(tr, batch, w):
     groups = touched[: (touched.size // per_q) * per_q].reshape(-1, per_q).any(1)
     active = int(groups.sum())
     tb = 2 if w["table"] == "F16" else 0
-    nbytes = hc * 4 + touched.size + active * 4 * (24 + 4 + tb) + tr.mlp_count * 28
+    gb = 2 if grad == "F16" else 4        # gradient element (read and clear)
+    nbytes = hc * gb + touched.size + active * 4 * (24 + gb + tb) + tr.mlp_count * 28
     return {"bytes": nbytes, "active_fraction": active / max(groups.size, 1)}
 
 
@@ -356,7 +365,10 @@ def dp_parity_check(t, tr, rank, world, local):
        (cosine >= 0.999), and the slots that moved are the same;
     3. the same with int32 fixed-point gradients for one step: the summed
        hash gradient is exact in any order, so the hash table after the step
-       is bit-identical to the single-process one.
+       is bit-identical to the single-process one;
+    4. the replay of 2. with fp16 hash gradients (losses within 2e-3, weight
+       changes aligned to cosine >= 0.99: the ranks' fp16 partial sums are
+       added in another order than one process's reductions).
 
     This covers the 2-rank allreduce and, from 4 ranks, the reduce-scatter /
     shard Adam / all-gather update."""
@@ -422,9 +434,10 @@ def dp_parity_check(t, tr, rank, world, local):
     n = 4096
     h0, m0, h, m, la = dp_run("F32", 3, n)
     hf0, mf0, hf, mf, _ = dp_run("Fixed16", 1, n)
-    if rank == 0:
-        hs, ms, lb = single("F32", 3, n)
-        res["f32_3_steps"] = {
+    hh0, mh0, hh, mh, lh = dp_run("F16", 3, n)
+
+    def compare(h0, m0, h, m, la, hs, ms, lb):
+        return {
             "loss_max_rel": float(max(abs(x - y) / max(abs(y), 1e-30)
                                       for x, y in zip(la, lb))),
             "hash_delta_cosine": cos(h - h0, hs - h0),
@@ -432,6 +445,14 @@ def dp_parity_check(t, tr, rank, world, local):
             "moved_slots_mismatch": float(np.mean(
                 (h != h0).reshape(-1, 2).any(1) != (hs != h0).reshape(-1, 2).any(1))),
         }
+
+    if rank == 0:
+        hs, ms, lb = single("F32", 3, n)
+        res["f32_3_steps"] = compare(h0, m0, h, m, la, hs, ms, lb)
+        # fp16 gradients: the ranks' fp16 partial sums are added by NCCL in
+        # fp16, a different rounding order from one process's reductions
+        hs16, ms16, lb16 = single("F16", 3, n)
+        res["f16_3_steps"] = compare(hh0, mh0, hh, mh, lh, hs16, ms16, lb16)
         hsf, msf, _ = single("Fixed16", 1, n)
         res["fixed16_1_step"] = {
             "hash_bit_identical": bool(np.array_equal(hf.view(np.uint32),
@@ -443,6 +464,10 @@ def dp_parity_check(t, tr, rank, world, local):
               f["hash_delta_cosine"] >= 0.999 and f["mlp_delta_cosine"] >= 0.999
               and f["moved_slots_mismatch"] <= 1e-3 and
               res["fixed16_1_step"]["hash_bit_identical"])
+        f = res["f16_3_steps"]
+        ok = ok and (f["loss_max_rel"] <= 2e-3 and f["hash_delta_cosine"] >= 0.99
+                     and f["mlp_delta_cosine"] >= 0.99
+                     and f["moved_slots_mismatch"] <= 1e-3)
         res["status"] = "ok" if ok else "FAIL"
         res["path"] = "sharded optimizer (reduce-scatter, shard Adam, all-gather)" \
             if world >= 4 else "replicated optimizer (allreduce)"
@@ -933,7 +958,7 @@ def main():
                "h2d_bytes_per_step": int(hpool[0][0].nbytes + hpool[0][1].nbytes),
                "d2h_bytes_per_step": 8}
 
-    adam_bytes = adam_traffic_bytes(tr, pool[0], w)
+    adam_bytes = adam_traffic_bytes(tr, pool[0], w, args.grad)
     dp_parity = dp_parity_check(t, tr, rank, world, local) if world > 1 else None
     tr.close()
 
@@ -942,19 +967,28 @@ def main():
     # configs[4], the 8-GPU scaling target)
     subs = {}
     if not args.no_subworkloads and w.get("kind") is None:
-        for name in ("image", "field4d"):
-            if name == args.workload:
+        # also the fp16 hash-gradient option (half the scatter, clear and
+        # exchange bytes) on the headline and 4D workloads
+        for name, grad in (("image", None), ("field4d", None),
+                           (args.workload, "F16"), ("field4d", "F16")):
+            if name == args.workload and grad is None:
                 continue
+            if grad == args.grad or (name == "field4d" and grad and
+                                     args.workload == "field4d"
+                                     and name + "_grad_f16" in subs):
+                continue
+            key = name + ("_grad_f16" if grad == "F16" else "")
             r = time_training(t, name, args, rank, world, local,
                               steps=min(args.steps, 40), warmup=5,
-                              phase_steps=10)
+                              phase_steps=10, grad=grad)
             r["trainer"].close()
-            subs[name] = {k: r[k] for k in ("value", "ms_per_step", "phase_ms",
-                                            "family", "final_loss",
-                                            "roofline")}
-            subs[name]["unit"] = unit
-            subs[name]["desc"] = WORKLOADS[name]["desc"]
-            subs[name]["samples_per_s"] = r["value"] * WORKLOADS[name]["batch"]
+            subs[key] = {k: r[k] for k in ("value", "ms_per_step", "phase_ms",
+                                           "family", "final_loss",
+                                           "roofline")}
+            subs[key]["unit"] = unit
+            subs[key]["desc"] = WORKLOADS[name]["desc"]
+            subs[key]["hash_grad_format"] = grad or args.grad
+            subs[key]["samples_per_s"] = r["value"] * WORKLOADS[name]["batch"]
             del r
             torch.cuda.empty_cache()
 

@@ -69,9 +69,18 @@ typedef enum tmnn_family {
 
 /* Hash-table gradient format.  FIXED16 is the reference's int32 fixed point
  * (int(d*w*65536), truncation; mlp_kernel_emitter.cpp:20, :735-738).  F32 is
- * a float accumulator for batches where 2^-16 quantisation underflows. */
-typedef enum tmnn_grad_format { TMNN_GRAD_FIXED16 = 0, TMNN_GRAD_F32 = 1 }
-    tmnn_grad_format;
+ * a float accumulator for batches where 2^-16 quantisation underflows.  F16
+ * accumulates d*w*2^18 in fp16 with fp16x2 vector reductions (half the
+ * scatter, clear and exchange bytes of F32); a slot's summed gradient must
+ * stay below 65504 / 2^18 = 0.25 in magnitude (an overflow is an Inf that the
+ * numerics guard reports).  F16 runs in the tensor-core families (FullyFused,
+ * Tiled) and in SafeDebug; the buffer view of TMNN_BUF_GRAD_HASH is then
+ * dtype 1 (fp16) holding the scaled values. */
+typedef enum tmnn_grad_format {
+  TMNN_GRAD_FIXED16 = 0,
+  TMNN_GRAD_F32 = 1,
+  TMNN_GRAD_F16 = 2
+} tmnn_grad_format;
 
 typedef enum tmnn_dtype { TMNN_DTYPE_F32 = 0, TMNN_DTYPE_F16 = 1 } tmnn_dtype;
 
@@ -131,7 +140,14 @@ typedef struct tmnn_train_cfg {
                                      code (1..32); 0 = the whole code (30 bits
                                      in 3D, 32 in 4D, the reference's order up
                                      to ties).  Default 12. */
-  int32_t reserved[2];
+  int32_t enable_probes;          /* TrainerConfig::enable_probes
+                                     (include/tiny-metal-nn/trainer.h:51-54):
+                                     1 = per-step activation / gradient
+                                     telemetry (tmnn_cuda_last_probe).  Like
+                                     the reference, which then runs its scalar
+                                     training kernel, training steps run the
+                                     fp32 reference-order kernels. */
+  int32_t reserved;
 } tmnn_train_cfg;
 
 /* NumericsSamplingMode (runtime_policy.h:13-18). */
@@ -184,6 +200,22 @@ typedef struct tmnn_step_result {
   int32_t has_numerics_anomaly;
   int32_t recovery_action;    /* tmnn_recovery_action */
 } tmnn_step_result;
+
+/* ProbeResult (include/tiny-metal-nn/common.h:78-94): statistics of the
+ * last forward/backward pass with enable_probes set, over the points of this
+ * rank.  act_max[l] = max |activation| of hidden layer l; grad_l2[l] = sum
+ * over points of |dL/d(pre-activation of layer l)|^2; output_abs_max = max
+ * |output|; output_min = min(0, min output) for one output and 0 otherwise
+ * (the reference's TG reduction starts at 0); hash_grad_l2 stays 0 as in the
+ * reference, whose kernel never accumulates it. */
+typedef struct tmnn_probe_result {
+  uint32_t num_hidden_layers;
+  int32_t has_nan_forward, has_nan_backward;
+  float hash_grad_l2;
+  float act_max[8];
+  float grad_l2[8];
+  float output_abs_max, output_min;
+} tmnn_probe_result;
 
 /* Counters of the numerics guard (context_record_training_step,
  * training_step_execution.cpp:1047-1058). */
@@ -434,6 +466,12 @@ tmnn_status tmnn_cuda_get_buffer(tmnn_ctx *ctx, int32_t role,
  * bytes must equal the buffer's size. */
 tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *ctx, int32_t role, void *host,
                                   size_t bytes);
+/* TrainingStepResult::probe / ITrainerRuntime::read_last_split_probe
+ * (include/tiny-metal-nn/trainer.h:178-181, :363-366): the probe of the last
+ * training_step or forward_backward.  TMNN_ERR_INVALID_ARGUMENT when
+ * enable_probes is off, TMNN_ERR_OPERATION_FAILED when no pass ran yet (the
+ * reference returns nullopt in both cases). */
+tmnn_status tmnn_cuda_last_probe(tmnn_ctx *ctx, tmnn_probe_result *probe);
 /* NetworkPlan of the context (network_planner.cpp:132-290). */
 tmnn_status tmnn_cuda_get_plan(tmnn_ctx *ctx, tmnn_plan *plan);
 /* The context's CUDA stream (cudaStream_t) for interop. */

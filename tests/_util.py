@@ -19,7 +19,8 @@ def cuda_trainer(L=16, F=2, log2T=19, d=3, W=64, H=1, O=1, loss=0, base=16.0,
     cfg = _abi.TrainCfg()
     t.lib.tmnn_cuda_default_train_cfg(cfg)
     cfg.family = _abi.FAMILY[family]
-    cfg.hash_grad_format = _abi.GRAD_FIXED16 if grad == "Fixed16" else _abi.GRAD_F32
+    cfg.hash_grad_format = {"Fixed16": _abi.GRAD_FIXED16, "F32": _abi.GRAD_F32,
+                            "F16": _abi.GRAD_F16}[grad]
     cfg.morton_sort = 1 if morton else 0
     cfg.seed = seed
     cfg.lr_encoding = lr_enc

@@ -97,11 +97,25 @@ def _create(cfg_json, n_in=3, n_out=1):
     ('{"b200": {"bad_step_recovery": "Retry"}}', "allowed: SignalOnly, Throw"),
     ('{"b200": {"numerics_sampling_mode": "Often"}}', "allowed: Sampled"),
     ('{"b200": {"morton_key_bits": 40}}', "b200.morton_key_bits: must be in [0, 32]"),
+    ('{"b200": {"hash_grad_format": "BF16"}}', "allowed: Fixed16, F32, F16"),
+    ('{"b200": {"enable_probes": 2}}', "b200.enable_probes"),
 ])
 def test_config_errors_reported_without_gpu(cfg, frag):
     st, msg, _ = _create(cfg)
     assert st == 1, (st, msg)
     assert frag in msg, msg
+
+
+@pytest.mark.parametrize("b200", ['{"hash_grad_format": "F16"}',
+                                  '{"enable_probes": true}'])
+def test_new_b200_keys_parse_without_gpu(b200):
+    """The fp16 gradient format and the probe switch parse (creation then
+    fails only for want of a device)."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    st, msg, _ = _create('{"b200": %s}' % b200)
+    assert st != 0 and "device" in msg.lower(), msg
 
 
 def test_valid_config_fails_cleanly_without_gpu():

@@ -66,8 +66,11 @@ def test_tiled_features_and_fixed_point_gradients_equal_fused(kw):
     assert np.array_equal(a.read_buffer(21), b.read_buffer(21))    # touched
     assert rel(a.read_buffer(4), b.read_buffer(4)) <= 1e-5
     assert abs(la - lb) <= 1e-5 * abs(lb)
+    # inference: the Tiled family runs the pipelined MLP kernel, which adds
+    # the bias inside the MMA; a last-bit difference of a pre-activation can
+    # flip the fp16 rounding of a hidden activation (2^-11 relative)
     ya, yb = a.inference(pos), b.inference(pos)
-    assert np.abs(ya - yb).max() <= 1e-5 * max(np.abs(yb).max(), 1e-3)
+    assert np.abs(ya - yb).max() <= 2e-3 * max(np.abs(yb).max(), 1e-3)
     a.close()
     b.close()
 

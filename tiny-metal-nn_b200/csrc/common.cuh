@@ -8,7 +8,7 @@
 //           (mlp_kernel_emitter.cpp:163-191).
 //   m, v    f32, same shape (Adam moments of the fused [hash|mlp] buffer).
 //   table_h f16 [hash_count]  gather copy of the hash part (table_dtype F16).
-//   grad_hash  i32 fixed point (x 2^16) or f32 [hash_count].
+//   grad_hash  i32 fixed point (x 2^16), f32, or f16 (x 2^18) [hash_count].
 //   grad_mlp   f32 [mlp_count].
 //   touched    u8 per tracked slot (a feature pair when F == 2, else one
 //              element): the reference's active-hash bitmask
@@ -24,6 +24,11 @@ constexpr int kMaxLevels = 32;
 constexpr int kMaxHidden = 8;
 constexpr float kGradScale = 65536.0f;  // mlp_kernel_emitter.cpp:20
 constexpr float kInvGradScale = 1.0f / 65536.0f;
+// fp16 hash gradients hold d*w*2^18: per-slot sums of mean-loss gradients
+// at the benchmark batches lie within ~1e-10..5e-4, so the scaled values are
+// mostly normal fp16 numbers with >2^17 headroom below the fp16 maximum
+constexpr float kHalfGradScale = 262144.0f;
+constexpr float kInvHalfGradScale = 1.0f / 262144.0f;
 
 // hash primes (mlp_kernel_emitter.cpp:16-18)
 constexpr uint32_t kPrimeY = 2654435761u;
@@ -37,6 +42,7 @@ struct NetDims {
   float huber_delta;     // already rounded to 6 decimals
   int32_t active_levels; // levels receiving gradients
   int32_t grad_fixed;    // 1: int32 fixed-point hash gradients
+  int32_t grad_half;     // 1: fp16 hash gradients (x kHalfGradScale)
   uint32_t T;            // 1 << log2T
   uint32_t mlp_count;
   uint64_t hash_count;
@@ -79,6 +85,17 @@ struct StepStats {
   int32_t gate;           // 1: Adam skips the update on an anomaly
 };
 
+// In-kernel training probes (ProbeResult, include/tiny-metal-nn/common.h:
+// 78-94), accumulated by the fp32 training kernel over all its points:
+// maxima of non-negative values (atomicMax on the float bits) and sums.
+struct ProbeAcc {
+  float fwd_nan, bwd_nan;   // 1 when a NaN was seen
+  float out_abs_max;        // max |output|
+  float out_neg_min;        // max(0, max -output), one-output networks
+  float act_max[kMaxHidden];
+  float grad_l2[kMaxHidden];
+};
+
 struct AdamArgs {
   float lr_hash, lr_mlp, beta1, beta2, eps, bc1, bc2, l1_hash, l2_mlp,
       grad_clip, weight_decay;
@@ -88,6 +105,7 @@ struct AdamArgs {
   int32_t entry_width;  // elements per tracked slot
   int32_t sparse;       // update only touched hash slots
   int32_t grad_fixed;
+  int32_t grad_half;       // gh_float points at fp16 values x kHalfGradScale
   int32_t implicit_touch;  // touched = byte set or nonzero float gradient
   const StepStats *guard;  // non-null: skip the update when the gated probe
                            // found an anomaly (gradients are still cleared)

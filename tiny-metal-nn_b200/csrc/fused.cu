@@ -595,11 +595,12 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
               if (P.implicit_touch && zero) {
                 // an all-zero contribution still touches its slot: it adds
                 // the smallest normal float 2^-126 (float reductions flush
-                // subnormals), so the slot's sum is nonzero and Adam treats
-                // it as touched; the value is below any weight's ulp
+                // subnormals; the fp16 reductions mark by themselves), so
+                // the slot's sum is nonzero and Adam treats it as touched;
+                // the value is below any weight's ulp
 #pragma unroll
                 for (int q = 0; q < F; ++q)
-                  gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(0x00800000);
+                  gv[q] = (F == 2 && q == 1) ? 0.f : touch_mark(nd.grad_half);
               }
               if (F == 2 && nd.res[l] <= kAggMaxRes) {
                 // warp aggregation: lanes with the same corner hand their
@@ -616,16 +617,13 @@ __global__ void __launch_bounds__(128 * Q, 8 / Q)
                     a += sa[2 * s];
                     b += sa[2 * s + 1];
                   }
-                  red_add_f32x2(P.gh_float + off, a, b);
+                  const float ab[2] = {a, b};
+                  red_grad<2>(P.gh_float, nd.grad_half, off, ab);
                 }
                 __syncwarp(vmask);
-              } else if (F == 2)
-                red_add_f32x2(P.gh_float + off, gv[0], gv[F - 1]);
-              else if (F == 4)
-                red_add_f32x4(P.gh_float + off, gv[0], gv[1 % F], gv[2 % F],
-                              gv[3 % F]);
-              else
-                atomicAdd(P.gh_float + off, gv[0]);
+              } else {
+                red_grad<F>(P.gh_float, nd.grad_half, off, gv);
+              }
               if (P.implicit_touch) continue;
             }
             if (F == 2)
@@ -771,6 +769,7 @@ struct PipeParams {
   int *err;
   uint32_t N, ntiles;
   uint32_t bar_off;
+  uint32_t bias_off;    // bias slabs (per layer) and the ones operand
   uint32_t gcols;       // TMEM columns per tile (accumulator + A operand)
   uint32_t tcols;       // allocated TMEM columns
   int out_act;
@@ -785,12 +784,12 @@ __device__ __forceinline__ void mbar_arrive(uint32_t mbar) {
 // core-blocked MN-major shared-memory operand; one thread issues.
 __device__ __forceinline__ void gemm_ta(uint32_t tmem_d, uint32_t a_tmem,
                                         uint32_t b_base, int b_cols, int N,
-                                        int K) {
+                                        int K, bool accumulate = false) {
   const uint32_t id = tc::idesc(kTile, N, 0, 1);
   const uint32_t b_l = (uint32_t)b_cols * 16u, b_s = 128u;
   for (int s = 0; s < K / 16; ++s) {
     const uint64_t bd = tc::sdesc(b_base + s * 2u * b_l, b_l, b_s);
-    const uint32_t acc = s > 0 ? 1u : 0u;
+    const uint32_t acc = (s > 0 || accumulate) ? 1u : 0u;
     asm volatile(
         "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
@@ -825,6 +824,22 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t *>(&h);
 }
+// fp16 pair {relu(a) low, relu(b) high}, round to nearest: one instruction
+__device__ __forceinline__ uint32_t pack_relu_h2(float a, float b) {
+  uint32_t u;
+  asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;" : "=r"(u) : "f"(b), "f"(a));
+  return u;
+}
+
+// Bias slabs of the pipelined kernel: per layer a K = 16 MN-major operand
+// [16 x N] whose row 0 holds the fp16 rounding of the bias and row 1 the
+// fp16 rounding of the remainder (bias = hi + lo to ~2^-22 relative), and a
+// K-major ones operand [128 x 16] with ones in columns 0 and 1: the MMA
+// ones . slab starts every accumulator at the bias, so the epilogue only
+// applies ReLU and packs.
+__device__ __forceinline__ uint32_t pipe_slab_bytes(int W) {
+  return 16u * (uint32_t)(W > kOutCols ? W : kOutCols) * 2u;
+}
 
 // S = 2 splits each tile's epilogue over two warpgroups (one half of the
 // columns each), halving the epilogue's share of the per-layer chain.
@@ -842,6 +857,31 @@ __global__ void __launch_bounds__(128 + 128 * NG * S)
     const uint4 *src = reinterpret_cast<const uint4 *>(P.wimage);
     uint4 *dst = reinterpret_cast<uint4 *>(sm);
     for (uint32_t i = t; i < Ly.image_bytes / 16; i += blockDim.x) dst[i] = src[i];
+    // bias slabs from the biases in global memory (the image copy above
+    // may still be in flight), then the ones operand
+    const uint32_t slab = pipe_slab_bytes(W);
+    const float *gimg = reinterpret_cast<const float *>(P.wimage);
+    for (int k = 0; k <= H; ++k) {
+      const int n = k < H ? W : kOutCols;
+      __half *sl = reinterpret_cast<__half *>(sm + P.bias_off + (uint32_t)k * slab);
+      for (int i = t; i < 16 * n; i += blockDim.x) {
+        const int kr = i / n, c = i % n;
+        float v = 0.f;
+        if (kr < 2) {
+          const float b = gimg[Ly.b[k] / 4 + c];
+          const __half hi = __float2half_rn(b);
+          v = kr == 0 ? __half2float(hi) : b - __half2float(hi);
+        }
+        sl[tc::cb(kr, c, n)] = __float2half_rn(v);
+      }
+    }
+    {
+      __half *ones = reinterpret_cast<__half *>(sm + P.bias_off + (uint32_t)(H + 1) * slab);
+      for (int i = t; i < kTile * 16; i += blockDim.x) {
+        const int r = i / 16, c = i % 16;
+        ones[tc::cb(r, c, 16)] = __float2half_rn(c < 2 ? 1.f : 0.f);
+      }
+    }
     if (t < NG) {
       tc::mbar_init(tc::smem_u32(bars + t), 1);         // mma_done[g]
       tc::mbar_init(tc::smem_u32(bars + NG + t), 128 * S);  // act_ready[g]
@@ -887,10 +927,15 @@ __global__ void __launch_bounds__(128 + 128 * NG * S)
           const int k = layer[g];
           const uint32_t acc = tmem + (uint32_t)g * P.gcols;
           const uint32_t a = acc + (uint32_t)W;
+          const int n = k < H ? W : kOutCols;
+          const uint32_t slab = sbase + P.bias_off + (uint32_t)k * pipe_slab_bytes(W);
+          const uint32_t ones = sbase + P.bias_off + (uint32_t)(H + 1) * pipe_slab_bytes(W);
+          tc::gemm(acc, tc::Operand{ones, 16, 0}, tc::Operand{slab, n, 1}, kTile,
+                   n, 16, 0);
           if (k < H)
-            gemm_ta(acc, a, sbase + Ly.w[k], W, W, k == 0 ? In : W);
+            gemm_ta(acc, a, sbase + Ly.w[k], W, W, k == 0 ? In : W, true);
           else
-            gemm_ta(acc, a, sbase + Ly.w[H], kOutCols, kOutCols, W);
+            gemm_ta(acc, a, sbase + Ly.w[H], kOutCols, kOutCols, W, true);
           tc::commit(tc::smem_u32(bars + g));
           if (k == H) {
             layer[g] = 0;
@@ -977,7 +1022,6 @@ __global__ void __launch_bounds__(128 + 128 * NG * S)
         ph ^= 1u;
         tc::fence_after_sync();
         if (k < H) {
-          const float4 *bk = reinterpret_cast<const float4 *>(sm + Ly.b[k]);
           constexpr int WP = W / S;               // this part's columns
           constexpr int CHM = 32;  // register budget (the prefetched input row)
           constexpr int CH = WP < CHM ? WP : CHM; // columns per TMEM load wait
@@ -993,12 +1037,7 @@ __global__ void __launch_bounds__(128 + 128 * NG * S)
               tc::tmem_ld16(acc + c0, v);
             uint32_t hpk[CH / 2];
 #pragma unroll
-            for (int i = 0; i < CH; i += 4) {
-              const float4 b = bk[(c0 + i) / 4];
-              hpk[i / 2] = pack_h2(fmaxf(v[i] + b.x, 0.f), fmaxf(v[i + 1] + b.y, 0.f));
-              hpk[i / 2 + 1] =
-                  pack_h2(fmaxf(v[i + 2] + b.z, 0.f), fmaxf(v[i + 3] + b.w, 0.f));
-            }
+            for (int i = 0; i < CH; i += 2) hpk[i / 2] = pack_relu_h2(v[i], v[i + 1]);
 #pragma unroll
             for (int q = 0; q < CH / 2; q += 8)
               tmem_st8(a_cols + (uint32_t)(c0 / 2 + q), hpk + q);
@@ -1010,11 +1049,9 @@ __global__ void __launch_bounds__(128 + 128 * NG * S)
           float y[kOutCols];
           tc::tmem_ld16(acc, y);
           tc::fence_before_sync();
-          const float *bo = reinterpret_cast<const float *>(sm + Ly.b[H]);
+          if (P.out_act == 1) {
 #pragma unroll
-          for (int m = 0; m < kOutCols; ++m) {
-            y[m] += bo[m];
-            if (P.out_act == 1) y[m] = 1.0f / (1.0f + expf(-y[m]));
+            for (int m = 0; m < kOutCols; ++m) y[m] = 1.0f / (1.0f + expf(-y[m]));
           }
           if (valid) {
             float *o = P.out + (size_t)row * O;
@@ -1053,9 +1090,16 @@ uint32_t pipe_gcols(const NetDims &nd) {
 
 // Tiles in flight: as many as TMEM holds, 2..6; 0 when the weights do not
 // fit in shared memory.
+// Shared memory past the weight image: barriers and TMEM slot (128 bytes),
+// one bias slab per layer and the ones operand.
+uint32_t pipe_extra(const NetDims &nd) {
+  const uint32_t slab = 16u * (uint32_t)(nd.W > kOutCols ? nd.W : kOutCols) * 2u;
+  return 128u + (uint32_t)(nd.H + 1) * slab + kTile * 16u * 2u;
+}
+
 int pipe_groups(const NetDims &nd) {
   const Layout L = make_layout(nd, false);
-  if (align128(L.image_bytes) + 128 > kPipeSmemMax) return 0;
+  if (align128(L.image_bytes) + pipe_extra(nd) > kPipeSmemMax) return 0;
   int ng = (int)(512 / pipe_gcols(nd));
   if (ng > 6) ng = 6;
   if (nd.W >= 64 && ng > 4) ng = 4;  // measured: more tiles do not help there
@@ -1064,7 +1108,7 @@ int pipe_groups(const NetDims &nd) {
 
 uint32_t pipe_smem(const NetDims &nd) {
   if (!pipe_groups(nd)) return 0;
-  return align128(make_layout(nd, false).image_bytes) + 128;
+  return align128(make_layout(nd, false).image_bytes) + pipe_extra(nd);
 }
 
 int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
@@ -1093,6 +1137,7 @@ int launch_mlp_pipe(FusedWorkspace &ws, const NetDims &nd, const float *mlp,
   int NG = pipe_groups(nd);
   if (split == 2 && NG > 3) NG = 3;
   P.bar_off = align128(P.lay.image_bytes);
+  P.bias_off = P.bar_off + 128u;
   P.gcols = pipe_gcols(nd);
   P.tcols = 32;
   while (P.tcols < (uint32_t)NG * P.gcols) P.tcols <<= 1;

@@ -108,4 +108,72 @@ __device__ __forceinline__ void red_add_f32x4(float *addr, float a, float b,
       : "memory");
 }
 
+// fp16 hash-gradient reductions of values already scaled by
+// kHalfGradScale (noftz keeps subnormal sums).  A contribution whose fp16
+// rounding is all zero adds the smallest subnormal 2^-24 instead (true
+// scale 2^-42), so every slot that received a contribution holds a nonzero
+// sum: the implicit touch mark of the float formats, which Adam reads as
+// "touched", and below any weight's ulp.
+__device__ __forceinline__ uint32_t half2_bits_marked(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  uint32_t u = *reinterpret_cast<const uint32_t *>(&h);
+  if ((u & 0x7fff7fffu) == 0u) u = 0x00000001u;
+  return u;
+}
+__device__ __forceinline__ void red_add_f16x2(__half *addr, float a, float b) {
+  asm volatile("red.relaxed.gpu.global.add.noftz.f16x2 [%0], %1;" ::"l"(addr),
+               "r"(half2_bits_marked(a, b))
+               : "memory");
+}
+__device__ __forceinline__ void red_add_f16x4(__half *addr, float a, float b,
+                                              float c, float d) {
+  const __half2 h0 = __floats2half2_rn(a, b), h1 = __floats2half2_rn(c, d);
+  uint32_t u0 = *reinterpret_cast<const uint32_t *>(&h0);
+  const uint32_t u1 = *reinterpret_cast<const uint32_t *>(&h1);
+  if (((u0 | u1) & 0x7fff7fffu) == 0u) u0 = 0x00000001u;
+  asm volatile("red.relaxed.gpu.global.add.noftz.v2.f16x2 [%0], {%1, %2};" ::"l"(addr),
+               "r"(u0), "r"(u1)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_f16(__half *addr, float a) {
+  const __half h = __float2half_rn(a);
+  uint16_t u = *reinterpret_cast<const uint16_t *>(&h);
+  if ((u & 0x7fffu) == 0u) u = 0x0001u;
+  asm volatile("red.relaxed.gpu.global.add.noftz.f16 [%0], %1;" ::"l"(addr),
+               "h"(u)
+               : "memory");
+}
+
+// Implicit touch mark of an all-zero contribution to the fp32 format: the
+// smallest normal float (float reductions flush subnormals).  The fp16
+// format marks inside its reductions (above), so it needs none here.
+__device__ __forceinline__ float touch_mark(int half) {
+  return half ? 0.0f : __int_as_float(0x00800000);
+}
+
+// One corner's float contribution gv[F] (true scale) into the hash
+// gradients at element off: fp32 vector reductions, or fp16 ones of the
+// values times kHalfGradScale when half is set (gh then holds __half).
+template <int F>
+__device__ __forceinline__ void red_grad(float *gh, bool half, uint32_t off,
+                                         const float *gv) {
+  if (half) {
+    __half *hp = reinterpret_cast<__half *>(gh) + off;
+    if (F == 2)
+      red_add_f16x2(hp, gv[0] * kHalfGradScale, gv[F - 1] * kHalfGradScale);
+    else if (F == 4)
+      red_add_f16x4(hp, gv[0] * kHalfGradScale, gv[1 % F] * kHalfGradScale,
+                    gv[2 % F] * kHalfGradScale, gv[3 % F] * kHalfGradScale);
+    else
+      red_add_f16(hp, gv[0] * kHalfGradScale);
+    return;
+  }
+  if (F == 2)
+    red_add_f32x2(gh + off, gv[0], gv[F - 1]);
+  else if (F == 4)
+    red_add_f32x4(gh + off, gv[0], gv[1 % F], gv[2 % F], gv[3 % F]);
+  else
+    atomicAdd(gh + off, gv[0]);
+}
+
 }  // namespace tmnn

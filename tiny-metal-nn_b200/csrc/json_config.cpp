@@ -389,7 +389,7 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
   known_keys(b2, {"family", "hash_grad_format", "table_dtype", "morton_sort",
                   "sparse_hash_adam", "active_levels", "numerics_sampling_mode",
                   "numerics_sample_interval", "bad_step_recovery",
-                  "morton_key_bits"},
+                  "morton_key_bits", "enable_probes"},
              "b200", d);
   const std::string fam = str(b2, "family", "Auto", "b200.family", d);
   if (fam == "Auto") cfg->family = TMNN_FAMILY_AUTO;
@@ -402,8 +402,9 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
                              "b200.hash_grad_format", d);
   if (gf == "Fixed16") cfg->hash_grad_format = TMNN_GRAD_FIXED16;
   else if (gf == "F32") cfg->hash_grad_format = TMNN_GRAD_F32;
+  else if (gf == "F16") cfg->hash_grad_format = TMNN_GRAD_F16;
   else d.err("b200.hash_grad_format", "unsupported value '" + gf +
-                                          "'; allowed: Fixed16, F32");
+                                          "'; allowed: Fixed16, F32, F16");
   const std::string td = str(b2, "table_dtype", "F32", "b200.table_dtype", d);
   if (td == "F32") spec->table_dtype = TMNN_DTYPE_F32;
   else if (td == "F16") spec->table_dtype = TMNN_DTYPE_F16;
@@ -413,6 +414,9 @@ void config_from_json(uint32_t n_input, uint32_t n_output, const char *text,
     cfg->sparse_hash_adam =
         boolean(b2, "sparse_hash_adam", true, "b200.sparse_hash_adam", d) ? 1 : 0;
   cfg->active_levels = integer(b2, "active_levels", 0, "b200.active_levels", d);
+  // TrainerConfig::enable_probes (include/tiny-metal-nn/trainer.h:51-54)
+  cfg->enable_probes =
+      boolean(b2, "enable_probes", false, "b200.enable_probes", d) ? 1 : 0;
   if (b2.get("morton_key_bits")) {
     const int kb = integer(b2, "morton_key_bits", 12, "b200.morton_key_bits", d);
     if (kb < 0 || kb > 32)

@@ -16,7 +16,7 @@ void launch_train_exact(const NetDims &nd, const float *table,
                         const float *dext, float inv_N, float *grad_mlp,
                         int32_t *gh_fixed, float *gh_float, uint8_t *touched,
                         double *loss_acc, uint32_t N, float *scratch,
-                        int num_sms, cudaStream_t st);
+                        int num_sms, cudaStream_t st, ProbeAcc *probe = nullptr);
 void launch_forward_exact(const NetDims &nd, const float *table,
                           const float *mlp, const float *pos, float *out,
                           uint32_t N, float *scratch, int num_sms,
@@ -42,7 +42,8 @@ void launch_numerics_probe(const AdamArgs &a, const float *w, const float *m,
                            uint64_t mlp_base, StepStats *st, int force,
                            int gate, int num_sms, cudaStream_t st_);
 void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
-                               int entry_width, int num_sms, cudaStream_t st);
+                               int entry_width, bool half, int num_sms,
+                               cudaStream_t st);
 void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,
                      float *gm, int num_sms, cudaStream_t st);
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,

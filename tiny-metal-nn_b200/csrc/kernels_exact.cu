@@ -131,6 +131,9 @@ __device__ inline void scatter_one(const NetDims &nd, const GradSink &g,
                                    uint32_t off, float v) {
   if (nd.grad_fixed)
     atomicAdd(g.gh_fixed + off, fixed_trunc(v * kGradScale));
+  else if (nd.grad_half)
+    atomicAdd(reinterpret_cast<__half *>(g.gh_float) + off,
+              __float2half_rn(v * kHalfGradScale));
   else
     atomicAdd(g.gh_float + off, v);
 }
@@ -216,6 +219,82 @@ __device__ void backward_point(const NetDims &nd, const float *table,
 // ------------------------------------------------------------ kernels
 
 
+// Probe statistics of one thread's points (the reference's emitted probe
+// code, mlp_kernel_emitter.cpp:2879-2886, :2993-3050, :3105-3155): forward
+// maxima and NaN flags after the forward pass, gradient sums of squares of
+// every hidden layer's pre-activation gradient after the backward pass.
+struct ProbeLocal {
+  float fwd_nan = 0.f, bwd_nan = 0.f, out_abs_max = 0.f, out_neg_min = 0.f;
+  float act_max[kMaxHidden] = {};
+  float grad_l2[kMaxHidden] = {};
+};
+
+__device__ void probe_forward(const NetDims &nd, const float *acts,
+                              const float *y, ProbeLocal &pl) {
+  for (int k = 0; k < nd.H; ++k)
+    for (int j = 0; j < nd.W; ++j) {
+      const float h = acts[k * nd.W + j];
+      pl.act_max[k] = fmaxf(pl.act_max[k], fabsf(h));
+      if (isnan(h)) pl.fwd_nan = 1.f;
+    }
+  if (nd.O == 1) {
+    // the reference assigns (one point per thread there): max over points
+    pl.out_abs_max = fmaxf(pl.out_abs_max, fabsf(y[0]));
+    pl.out_neg_min = fmaxf(pl.out_neg_min, -y[0]);
+    if (isnan(y[0])) pl.fwd_nan = 1.f;
+  } else {
+    for (int m = 0; m < nd.O; ++m) {
+      pl.out_abs_max = fmaxf(pl.out_abs_max, fabsf(y[m]));
+      if (isnan(y[m])) pl.fwd_nan = 1.f;
+    }
+  }
+}
+
+__device__ void probe_backward(const NetDims &nd, const float *dacts,
+                               const float *d, ProbeLocal &pl) {
+  for (int m = 0; m < nd.O; ++m)
+    if (isnan(d[m])) pl.bwd_nan = 1.f;
+  for (int k = 0; k < nd.H; ++k)
+    for (int j = 0; j < nd.W; ++j) {
+      const float g = dacts[k * nd.W + j];
+      pl.grad_l2[k] = pl.grad_l2[k] + g * g;
+      if (isnan(g)) pl.bwd_nan = 1.f;
+    }
+}
+
+__device__ __forceinline__ void probe_max(float *addr, float v) {
+  if (v > 0.f) atomicMax(reinterpret_cast<int *>(addr), __float_as_int(v));
+}
+
+// Warp reduction of the thread statistics, one set of atomics per warp.
+__device__ void probe_flush(const NetDims &nd, ProbeLocal &pl, ProbeAcc *acc) {
+  const unsigned full = 0xffffffffu;
+  auto wmax = [&](float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(full, v, o));
+    return v;
+  };
+  auto wsum = [&](float v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(full, v, o);
+    return v;
+  };
+  const bool lead = (threadIdx.x & 31) == 0;
+  const float fn = wmax(pl.fwd_nan), bn = wmax(pl.bwd_nan);
+  const float oa = wmax(pl.out_abs_max), on = wmax(pl.out_neg_min);
+  if (lead) {
+    probe_max(&acc->fwd_nan, fn);
+    probe_max(&acc->bwd_nan, bn);
+    probe_max(&acc->out_abs_max, oa);
+    probe_max(&acc->out_neg_min, on);
+  }
+  for (int k = 0; k < nd.H; ++k) {
+    const float am = wmax(pl.act_max[k]), gs = wsum(pl.grad_l2[k]);
+    if (lead) {
+      probe_max(&acc->act_max[k], am);
+      if (gs != 0.f) atomicAdd(&acc->grad_l2[k], gs);
+    }
+  }
+}
+
 template <int WMAX>
 __global__ void __launch_bounds__(kExactBlock)
     k_train_exact(NetDims nd, const float *__restrict__ table,
@@ -223,7 +302,8 @@ __global__ void __launch_bounds__(kExactBlock)
                   const float *__restrict__ tgt, const float *__restrict__ dext,
                   float inv_N, float *grad_mlp, int32_t *gh_fixed,
                   float *gh_float, uint8_t *touched, double *loss_acc,
-                  uint32_t N, int use_smem_grads, float *scratch) {
+                  uint32_t N, int use_smem_grads, float *scratch,
+                  ProbeAcc *probe) {
   extern __shared__ float s_grad[];
   __shared__ double s_loss[kExactBlock / 32];
   if (use_smem_grads) {
@@ -237,18 +317,24 @@ __global__ void __launch_bounds__(kExactBlock)
                          : scratch + (size_t)(blockIdx.x * blockDim.x +
                                               threadIdx.x) * nd.H * nd.W;
   float loss = 0.0f;
+  ProbeLocal pl;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < N;
        i += gridDim.x * blockDim.x) {
     const float *p = pos + (size_t)i * nd.d;
     float y[64], d[64];
     forward_point(nd, table, mlp, p, acts, y);
+    if (probe) probe_forward(nd, acts, y, pl);
     if (dext) {
       for (int m = 0; m < nd.O; ++m) d[m] = dext[(size_t)i * nd.O + m];
     } else {
       loss = loss + point_loss(nd, y, tgt + (size_t)i * nd.O, inv_N, d);
     }
     backward_point(nd, table, mlp, p, acts, d, g);
+    // backward_point leaves each hidden layer's pre-activation gradient in
+    // acts
+    if (probe) probe_backward(nd, acts, d, pl);
   }
+  if (probe) probe_flush(nd, pl, probe);
   // block loss reduction in double, one atomic per block
   double lv = loss;
   for (int o = 16; o > 0; o >>= 1) lv += __shfl_down_sync(0xffffffffu, lv, o);
@@ -352,6 +438,10 @@ __global__ void k_adam(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
         if (a.grad_fixed) {
           g = (float)gh_fixed[e] * kInvGradScale;
           gh_fixed[e] = 0;
+        } else if (a.grad_half) {
+          __half *gh = reinterpret_cast<__half *>(gh_float);
+          g = __half2float(gh[e]) * kInvHalfGradScale;
+          gh[e] = __float2half_rn(0.0f);
         } else {
           g = gh_float[e];
           gh_float[e] = 0.0f;
@@ -401,7 +491,7 @@ __device__ inline void adam_mlp_range(const AdamArgs &a, float *w, float *m,
 // accesses (the table size L*T*F is a multiple of 4), followed by the MLP
 // weights (gm non-null) in the same launch.  Same arithmetic per element as
 // k_adam.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 4)
     k_adam_hash4(AdamArgs a, float *__restrict__ w, float *__restrict__ m,
                  float *__restrict__ v, int32_t *gh_fixed, float *gh_float,
                  uint8_t *__restrict__ touched, __half *table_h, float *gm) {
@@ -418,48 +508,82 @@ __global__ void __launch_bounds__(256)
       }
       if (a.grad_fixed)
         reinterpret_cast<int4 *>(gh_fixed)[q] = make_int4(0, 0, 0, 0);
+      else if (a.grad_half)
+        reinterpret_cast<uint2 *>(gh_float)[q] = make_uint2(0u, 0u);
       else
         reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (gm) adam_mlp_range(a, w, m, v, gm, true);
     return;
   }
-  for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
-       q += (uint64_t)gridDim.x * blockDim.x) {
+  // Software-pipelined by one group: the touched bytes and gradients of
+  // the thread's next group are loaded before the current group's w, m, v
+  // are, so a gradient load is always in flight beside them.
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t tt = 0u;
+  int4 gi = make_int4(0, 0, 0, 0);
+  uint4 gf = make_uint4(0u, 0u, 0u, 0u);  // fp32 gradients (bits), or fp16 in .x, .y
+  auto load_next = [&](uint64_t qq, uint32_t &t_, int4 &i_, uint4 &f_) {
+    if (qq >= n4) return;
+    if (a.sparse)
+      t_ = a.entry_width == 2 ? (uint32_t)reinterpret_cast<uint16_t *>(touched)[qq]
+                              : reinterpret_cast<uint32_t *>(touched)[qq];
+    if (a.grad_fixed) {
+      i_ = reinterpret_cast<int4 *>(gh_fixed)[qq];
+    } else if (a.grad_half) {
+      const uint2 r = reinterpret_cast<uint2 *>(gh_float)[qq];
+      f_ = make_uint4(r.x, r.y, 0u, 0u);
+    } else {
+      f_ = reinterpret_cast<uint4 *>(gh_float)[qq];
+    }
+  };
+  load_next(q, tt, gi, gf);
+#pragma unroll 1
+  for (; q < n4; q += stride) {
+    const uint32_t tc = tt;
+    const int4 gic = gi;
+    const uint4 gfc = gf;
+    load_next(q + stride, tt, gi, gf);
     bool on[4] = {true, true, true, true};
     if (a.sparse) {
+      // touched bytes: one per pair (entry width 2) or per element
       if (a.entry_width == 2) {
-        uchar2 tt = reinterpret_cast<uchar2 *>(touched)[q];
-        on[0] = on[1] = tt.x != 0;
-        on[2] = on[3] = tt.y != 0;
-        if (tt.x | tt.y) reinterpret_cast<uchar2 *>(touched)[q] = make_uchar2(0, 0);
+        on[0] = on[1] = (tc & 0xffu) != 0;
+        on[2] = on[3] = (tc >> 8) != 0;
+        if (tc) reinterpret_cast<uint16_t *>(touched)[q] = 0;
       } else {
-        uchar4 tt = reinterpret_cast<uchar4 *>(touched)[q];
-        on[0] = tt.x != 0;
-        on[1] = tt.y != 0;
-        on[2] = tt.z != 0;
-        on[3] = tt.w != 0;
-        if (tt.x | tt.y | tt.z | tt.w)
-          reinterpret_cast<uchar4 *>(touched)[q] = make_uchar4(0, 0, 0, 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) on[k] = ((tc >> (8 * k)) & 0xffu) != 0;
+        if (tc) reinterpret_cast<uint32_t *>(touched)[q] = 0u;
       }
     }
     float g[4];
     if (a.grad_fixed) {
-      const int4 gi = reinterpret_cast<int4 *>(gh_fixed)[q];
-      g[0] = (float)gi.x * kInvGradScale;
-      g[1] = (float)gi.y * kInvGradScale;
-      g[2] = (float)gi.z * kInvGradScale;
-      g[3] = (float)gi.w * kInvGradScale;
-      if (gi.x | gi.y | gi.z | gi.w)
+      g[0] = (float)gic.x * kInvGradScale;
+      g[1] = (float)gic.y * kInvGradScale;
+      g[2] = (float)gic.z * kInvGradScale;
+      g[3] = (float)gic.w * kInvGradScale;
+      if (gic.x | gic.y | gic.z | gic.w)
         reinterpret_cast<int4 *>(gh_fixed)[q] = make_int4(0, 0, 0, 0);
     } else {
-      const float4 gf = reinterpret_cast<float4 *>(gh_float)[q];
-      g[0] = gf.x;
-      g[1] = gf.y;
-      g[2] = gf.z;
-      g[3] = gf.w;
-      if (gf.x != 0.f || gf.y != 0.f || gf.z != 0.f || gf.w != 0.f)
-        reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a.grad_half) {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&gfc.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&gfc.y));
+        g[0] = lo.x * kInvHalfGradScale;
+        g[1] = lo.y * kInvHalfGradScale;
+        g[2] = hi.x * kInvHalfGradScale;
+        g[3] = hi.y * kInvHalfGradScale;
+        // a subnormal fp16 touch mark scales to a nonzero float (2^-42)
+        if (gfc.x | gfc.y) reinterpret_cast<uint2 *>(gh_float)[q] = make_uint2(0u, 0u);
+      } else {
+        g[0] = __uint_as_float(gfc.x);
+        g[1] = __uint_as_float(gfc.y);
+        g[2] = __uint_as_float(gfc.z);
+        g[3] = __uint_as_float(gfc.w);
+        if (g[0] != 0.f || g[1] != 0.f || g[2] != 0.f || g[3] != 0.f)
+          reinterpret_cast<float4 *>(gh_float)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       if (a.sparse && a.implicit_touch) {
         if (a.entry_width == 2) {
           on[0] = on[1] = on[0] || g[0] != 0.f || g[1] != 0.f;
@@ -553,7 +677,10 @@ __global__ void __launch_bounds__(256)
     if (is_mlp)
       g = gm[i - a.hash_count];
     else
-      g = a.grad_fixed ? (float)gh_fixed[i] * kInvGradScale : gh_float[i];
+      g = a.grad_fixed  ? (float)gh_fixed[i] * kInvGradScale
+          : a.grad_half ? __half2float(reinterpret_cast<const __half *>(gh_float)[i]) *
+                              kInvHalfGradScale
+                        : gh_float[i];
     if (!isfinite(g)) {
       bad_g = true;
       continue;
@@ -615,20 +742,24 @@ void launch_numerics_probe(const AdamArgs &a, const float *w, const float *m,
 // Completes the touched map of the implicit-touch mode: a slot whose float
 // gradient is nonzero is touched (read-back only).
 __global__ void k_touched_from_grads(const float *__restrict__ g,
-                                     uint8_t *touched, uint64_t slots, int ew) {
+                                     uint8_t *touched, uint64_t slots, int ew,
+                                     int half) {
+  const __half *gh = reinterpret_cast<const __half *>(g);
   for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < slots;
        s += (uint64_t)gridDim.x * blockDim.x) {
     bool nz = false;
-    for (int k = 0; k < ew; ++k) nz = nz || g[s * ew + k] != 0.f;
+    for (int k = 0; k < ew; ++k)
+      nz = nz || (half ? __half2float(gh[s * ew + k]) != 0.f : g[s * ew + k] != 0.f);
     if (nz) touched[s] = 1;
   }
 }
 
 void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
-                               int entry_width, int num_sms, cudaStream_t st) {
+                               int entry_width, bool half, int num_sms,
+                               cudaStream_t st) {
   if (slots)
     k_touched_from_grads<<<num_sms * 8, 256, 0, st>>>(g, touched, slots,
-                                                      entry_width);
+                                                      entry_width, half ? 1 : 0);
 }
 
 __global__ void k_to_half(const float *__restrict__ src, __half *dst,
@@ -858,7 +989,7 @@ void launch_train_exact(const NetDims &nd, const float *table,
                         const float *dext, float inv_N, float *grad_mlp,
                         int32_t *gh_fixed, float *gh_float, uint8_t *touched,
                         double *loss_acc, uint32_t N, float *scratch,
-                        int num_sms, cudaStream_t st) {
+                        int num_sms, cudaStream_t st, ProbeAcc *probe) {
   if (N == 0) return;
   const int grid = exact_grid(N, num_sms);
   const size_t smem = (size_t)nd.mlp_count * sizeof(float);
@@ -872,7 +1003,7 @@ void launch_train_exact(const NetDims &nd, const float *table,
                            (int)dyn);                                         \
     k_train_exact<WM><<<grid, kExactBlock, dyn, st>>>(                        \
         nd, table, mlp, pos, tgt, dext, inv_N, grad_mlp, gh_fixed, gh_float,  \
-        touched, loss_acc, N, use_smem, scratch);                             \
+        touched, loss_acc, N, use_smem, scratch, probe);                      \
   }
   switch (wmax_for(nd.W)) {
     case 16: TMNN_TRAIN_CASE(16) break;

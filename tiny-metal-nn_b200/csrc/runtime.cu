@@ -150,6 +150,9 @@ struct tmnn_ctx {
   DevBuf<uint8_t> touched;
   DevBuf<double> loss_acc;  // a StepStats (loss first), see stats()
   DevBuf<float> scratch;
+  // enable_probes: statistics of the last forward/backward pass
+  DevBuf<float> probe;
+  bool probe_ran = false;
   // batch staging
   DevBuf<float> pos_in, tgt_in, pos_s, tgt_s, out_buf, out_s;
   DevBuf<float> grad_out, eg_scratch;  // evaluate_with_gradient
@@ -209,6 +212,17 @@ struct tmnn_ctx {
   bool tensor_core_family() const {
     return family == TMNN_FAMILY_FULLY_FUSED || family == TMNN_FAMILY_TILED;
   }
+  // the float-format hash gradients (fp32, or fp16 held in the same
+  // allocation) from element `off`, their element size and NCCL type
+  bool grad_half() const { return nd.grad_half != 0; }
+  float *ghf(uint64_t off) {
+    if (!gh_float.p) return nullptr;
+    return grad_half() ? reinterpret_cast<float *>(
+                             reinterpret_cast<__half *>(gh_float.p) + off)
+                       : gh_float.p + off;
+  }
+  size_t gh_elem() const { return grad_half() ? 2 : 4; }
+  ncclDataType_t gh_type() const { return grad_half() ? ncclFloat16 : ncclFloat32; }
 
   ~tmnn_ctx() {
     if (stream) cudaStreamSynchronize(stream);
@@ -388,6 +402,7 @@ NetDims make_dims(const tmnn_spec &s, const tmnn_train_cfg &c) {
   nd.active_levels =
       c.active_levels > 0 && c.active_levels < nd.L ? c.active_levels : nd.L;
   nd.grad_fixed = c.hash_grad_format == TMNN_GRAD_FIXED16 ? 1 : 0;
+  nd.grad_half = c.hash_grad_format == TMNN_GRAD_F16 ? 1 : 0;
   nd.T = 1u << nd.log2T;
   nd.hash_count = (uint64_t)nd.L * nd.T * nd.F;
   int64_t off = 0;
@@ -443,7 +458,16 @@ void plan_family(tmnn_ctx &c) {
            : w.find("output") != std::string::npos ? kReasonUnsupportedOutputDims
                                                    : kReasonUnsupportedInputDims;
   };
-  if (want == TMNN_FAMILY_SAFE_DEBUG) {
+  if (c.cfg.enable_probes) {
+    // TrainerConfig::enable_probes disables the reference's SIMD training
+    // kernels (include/tiny-metal-nn/trainer.h:51-54): the probes are
+    // emitted into its scalar kernel.  The same here: the fp32
+    // reference-order kernels carry them.
+    c.family = TMNN_FAMILY_SAFE_DEBUG;
+    c.fallback_reason = kReasonForcedSafeDebug;
+    c.plan_text = "SafeDebug: enable_probes (the probes ride in the fp32 "
+                  "reference-order training kernel)";
+  } else if (want == TMNN_FAMILY_SAFE_DEBUG) {
     c.family = TMNN_FAMILY_SAFE_DEBUG;
     c.fallback_reason = kReasonForcedSafeDebug;
     c.plan_text = "SafeDebug requested";
@@ -659,9 +683,15 @@ void fwd_bwd(tmnn_ctx &c, const float *pos, const float *tgt,
                               c.implicit_touch);
     return;
   }
+  ProbeAcc *pa = nullptr;
+  if (c.cfg.enable_probes) {
+    pa = reinterpret_cast<ProbeAcc *>(c.probe.p);
+    CK(cudaMemsetAsync(pa, 0, sizeof(ProbeAcc), c.stream));
+    c.probe_ran = true;
+  }
   launch_train_exact(c.nd, c.hash_w(), c.mlp_w(), pos, tgt, dext, inv_N,
                      c.gm.p, c.gh_fixed.p, c.gh_float.p, c.touched.p,
-                     c.loss_acc.p, N, c.scratch.p, c.num_sms, c.stream);
+                     c.loss_acc.p, N, c.scratch.p, c.num_sms, c.stream, pa);
   c.launches++;
 }
 
@@ -689,7 +719,7 @@ void allreduce_grads(tmnn_ctx &c, bool with_loss) {
     NK(ncclAllReduce(c.gh_fixed.p, c.gh_fixed.p, c.hash_count, ncclInt32,
                      ncclSum, c.comm, c.stream));
   else
-    NK(ncclAllReduce(c.gh_float.p, c.gh_float.p, c.hash_count, ncclFloat32,
+    NK(ncclAllReduce(c.gh_float.p, c.gh_float.p, c.hash_count, c.gh_type(),
                      ncclSum, c.comm, c.stream));
   NK(ncclAllReduce(c.gm.p, c.gm.p, c.mlp_count, ncclFloat32, ncclSum, c.comm,
                    c.stream));
@@ -725,6 +755,7 @@ AdamArgs adam_args(const tmnn_ctx &c) {
   a.entry_width = c.entry_width;
   a.sparse = c.sparse ? 1 : 0;
   a.grad_fixed = c.nd.grad_fixed;
+  a.grad_half = c.nd.grad_half;
   a.implicit_touch = c.implicit_touch ? 1 : 0;
   return a;
 }
@@ -854,8 +885,8 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
         NK(ncclReduceScatter(c.gh_fixed.p + b.e0, c.gh_fixed.p + own, gs,
                              ncclInt32, ncclSum, c.comm, cs));
       else
-        NK(ncclReduceScatter(c.gh_float.p + b.e0, c.gh_float.p + own, gs,
-                             ncclFloat32, ncclSum, c.comm, cs));
+        NK(ncclReduceScatter(c.ghf(b.e0), c.ghf(own), gs,
+                             c.gh_type(), ncclSum, c.comm, cs));
       if (exch_touched)
         NK(ncclReduceScatter(c.touched.p + b.e0 / w, c.touched.p + own / w,
                              gs / w, ncclUint8, ncclMax, c.comm, cs));
@@ -864,8 +895,8 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
         NK(ncclAllReduce(c.gh_fixed.p + b.e0, c.gh_fixed.p + b.e0, b.n,
                          ncclInt32, ncclSum, c.comm, cs));
       else
-        NK(ncclAllReduce(c.gh_float.p + b.e0, c.gh_float.p + b.e0, b.n,
-                         ncclFloat32, ncclSum, c.comm, cs));
+        NK(ncclAllReduce(c.ghf(b.e0), c.ghf(b.e0), b.n,
+                         c.gh_type(), ncclSum, c.comm, cs));
       if (exch_touched)
         NK(ncclAllReduce(c.touched.p + b.e0 / w, c.touched.p + b.e0 / w,
                          b.n / w, ncclUint8, ncclMax, c.comm, cs));
@@ -898,7 +929,7 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
     ah.mlp_count = 0;
     launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
                 c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
-                c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                c.ghf(off), c.gm.p,
                 c.touched.p + off / w, c.table_h.p ? c.table_h.p + off : nullptr,
                 c.num_sms, c.stream);
     c.launches++;
@@ -907,7 +938,7 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
       if (c.gh_fixed.p)
         CK(cudaMemsetAsync(c.gh_fixed.p + b.e0, 0, b.n * 4, c.stream));
       if (c.gh_float.p)
-        CK(cudaMemsetAsync(c.gh_float.p + b.e0, 0, b.n * 4, c.stream));
+        CK(cudaMemsetAsync(c.ghf(b.e0), 0, b.n * c.gh_elem(), c.stream));
       CK(cudaMemsetAsync(c.touched.p + b.e0 / w, 0, b.n / w, c.stream));
       // large buckets gather as soon as their Adam is done (overlapping the
       // next bucket's Adam); small ones in one grouped call at the end
@@ -962,7 +993,7 @@ void dp_finish_sharded(tmnn_ctx &c, const std::vector<Bucket> &bs,
     ah.mlp_count = 0;
     launch_adam(ah, c.params.p + off, c.m.p + off, c.v.p + off,
                 c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
-                c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                c.ghf(off), c.gm.p,
                 c.touched.p + off / w, c.table_h.p ? c.table_h.p + off : nullptr,
                 c.num_sms, c.stream);
     c.launches++;
@@ -1036,8 +1067,8 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
       NK(ncclReduceScatter(c.gh_fixed.p + b.e0, c.gh_fixed.p + own, gs,
                            ncclInt32, ncclSum, c.comm, c.stream));
     else
-      NK(ncclReduceScatter(c.gh_float.p + b.e0, c.gh_float.p + own, gs,
-                           ncclFloat32, ncclSum, c.comm, c.stream));
+      NK(ncclReduceScatter(c.ghf(b.e0), c.ghf(own), gs,
+                           c.gh_type(), ncclSum, c.comm, c.stream));
     if (c.sparse && !c.implicit_touch)
       NK(ncclReduceScatter(c.touched.p + b.e0 / w, c.touched.p + own / w,
                            gs / w, ncclUint8, ncclMax, c.comm, c.stream));
@@ -1059,7 +1090,7 @@ void dp_update(tmnn_ctx &c, bool with_loss, cudaEvent_t after_comm,
       if (i > 0) ap.mlp_count = 0;  // the MLP is scanned once
       launch_numerics_probe(ap, c.params.p + off, c.m.p + off, c.v.p + off,
                             c.gh_fixed.p ? c.gh_fixed.p + off : nullptr,
-                            c.gh_float.p ? c.gh_float.p + off : nullptr, c.gm.p,
+                            c.ghf(off), c.gm.p,
                             c.hash_count - off, c.stats(), 1, gate ? 1 : 0,
                             c.num_sms, c.stream);
       c.launches++;
@@ -1110,8 +1141,9 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
             const tmnn_train_cfg &cfg) {
   validate(spec);
   if (cfg.hash_grad_format != TMNN_GRAD_FIXED16 &&
-      cfg.hash_grad_format != TMNN_GRAD_F32)
-    throw std::invalid_argument("hash_grad_format must be FIXED16 or F32");
+      cfg.hash_grad_format != TMNN_GRAD_F32 &&
+      cfg.hash_grad_format != TMNN_GRAD_F16)
+    throw std::invalid_argument("hash_grad_format must be FIXED16, F32 or F16");
   if (cfg.batch_size <= 0) throw std::invalid_argument("batch_size must be > 0");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -1145,10 +1177,12 @@ void create(tmnn_ctx &c, int device, const tmnn_spec &spec,
   c.implicit_touch = c.tensor_core_family() && !c.nd.grad_fixed;
   if (c.nd.grad_fixed)
     c.gh_fixed.alloc(c.hash_count);
-  else
-    c.gh_float.alloc(c.hash_count);
+  else  // fp16 gradients share the float buffer (half its size)
+    c.gh_float.alloc(c.nd.grad_half ? (c.hash_count + 1) / 2 : c.hash_count);
   c.gm.alloc(c.mlp_count);
   c.touched.alloc(c.slots);
+  if (cfg.enable_probes)
+    c.probe.alloc((sizeof(ProbeAcc) + sizeof(float) - 1) / sizeof(float));
   static_assert(sizeof(StepStats) % sizeof(double) == 0, "StepStats size");
   c.loss_acc.alloc(sizeof(StepStats) / sizeof(double));
   c.guard.mode = cfg.numerics_sampling_mode;
@@ -1880,7 +1914,8 @@ tmnn_status tmnn_cuda_read_buffer(tmnn_ctx *c, int32_t role, void *host,
     CK(cudaSetDevice(c->device));
     if (role == TMNN_BUF_TOUCHED && c->implicit_touch)
       launch_touched_from_grads(c->gh_float.p, c->touched.p, c->slots,
-                                c->entry_width, c->num_sms, c->stream);
+                                c->entry_width, c->grad_half(), c->num_sms,
+                                c->stream);
     CK(cudaMemcpyAsync(host, v.device_ptr, bytes, cudaMemcpyDeviceToHost,
                        c->stream));
     CK(cudaStreamSynchronize(c->stream));
@@ -2100,6 +2135,35 @@ tmnn_status tmnn_cuda_get_step(tmnn_ctx *c, uint32_t *step) {
   return TMNN_OK;
 }
 
+tmnn_status tmnn_cuda_last_probe(tmnn_ctx *c, tmnn_probe_result *r) {
+  REQUIRE_CTX(c);
+  return guarded([&] {
+    if (!r) throw std::invalid_argument("last_probe: null result");
+    if (!c->cfg.enable_probes)
+      throw std::invalid_argument("last_probe: enable_probes is off");
+    if (!c->probe_ran)
+      throw std::runtime_error("last_probe: no forward/backward pass has run");
+    BusyGuard g(c);
+    CK(cudaSetDevice(c->device));
+    ProbeAcc a{};
+    CK(cudaMemcpyAsync(&a, c->probe.p, sizeof a, cudaMemcpyDeviceToHost,
+                       c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    // aggregate_probe_partials (training_step_execution.cpp:1326-1369)
+    std::memset(r, 0, sizeof *r);
+    r->num_hidden_layers = (uint32_t)c->nd.H;
+    r->has_nan_forward = a.fwd_nan > 0.f;
+    r->has_nan_backward = a.bwd_nan > 0.f;
+    r->hash_grad_l2 = 0.f;
+    r->output_abs_max = a.out_abs_max;
+    r->output_min = -a.out_neg_min;
+    for (int l = 0; l < c->nd.H && l < 8; ++l) {
+      r->act_max[l] = a.act_max[l];
+      r->grad_l2[l] = a.grad_l2[l];
+    }
+  });
+}
+
 tmnn_status tmnn_cuda_get_buffer(tmnn_ctx *c, int32_t role,
                                  tmnn_buffer_view *v) {
   REQUIRE_CTX(c);
@@ -2117,7 +2181,8 @@ tmnn_status tmnn_cuda_get_buffer(tmnn_ctx *c, int32_t role,
         if (c->gh_fixed.p)
           *v = {c->gh_fixed.p, c->gh_fixed.bytes(), 2};
         else
-          *v = {c->gh_float.p, c->gh_float.bytes(), 0};
+          *v = {c->gh_float.p, c->hash_count * c->gh_elem(),
+                c->grad_half() ? 1 : 0};
         break;
       case TMNN_BUF_GRAD_MLP:
         *v = {c->gm.p, c->gm.bytes(), 0};

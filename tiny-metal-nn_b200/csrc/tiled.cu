@@ -155,7 +155,8 @@ __global__ void __launch_bounds__(kThreads)
   if (nd.grad_fixed)
     prefetch_next_level(P, P.gh_fixed, (uint64_t)nd.T * F * 4, l, nd.active_levels);
   else
-    prefetch_next_level(P, P.gh_float, (uint64_t)nd.T * F * 4, l, nd.active_levels);
+    prefetch_next_level(P, P.gh_float, (uint64_t)nd.T * F * (nd.grad_half ? 2 : 4),
+                        l, nd.active_levels);
   const uint32_t i =
       (blockIdx.x % P.blocks_per_level) * kThreads + threadIdx.x;
   const bool valid = i < P.N;
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(kThreads)
         // slot's sum is nonzero; the value is below any weight's ulp
 #pragma unroll
         for (int q = 0; q < F; ++q)
-          gv[q] = (F == 2 && q == 1) ? 0.f : __int_as_float(0x00800000);
+          gv[q] = (F == 2 && q == 1) ? 0.f : touch_mark(nd.grad_half);
       }
       if (aggregate) {
         // lanes with the same corner hand their contributions to the lowest
@@ -224,15 +225,12 @@ __global__ void __launch_bounds__(kThreads)
             a += sa[2 * s];
             b += sa[2 * s + 1];
           }
-          red_add_f32x2(P.gh_float + off, a, b);
+          const float ab[2] = {a, b};
+          red_grad<2>(P.gh_float, nd.grad_half, off, ab);
         }
         __syncwarp(vmask);
-      } else if (F == 2) {
-        red_add_f32x2(P.gh_float + off, gv[0], gv[F - 1]);
-      } else if (F == 4) {
-        red_add_f32x4(P.gh_float + off, gv[0], gv[1 % F], gv[2 % F], gv[3 % F]);
       } else {
-        atomicAdd(P.gh_float + off, gv[0]);
+        red_grad<F>(P.gh_float, nd.grad_half, off, gv);
       }
       if (P.implicit_touch) continue;
     }

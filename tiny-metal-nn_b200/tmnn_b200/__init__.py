@@ -427,6 +427,24 @@ class Trainer:
                 "anomaly": bool(r.has_numerics_anomaly),
                 "recovery_action": _abi.RECOVERY_ACTION[r.recovery_action]}
 
+    def last_probe(self):
+        """ProbeResult of the last training_step / forward_backward (dict:
+        per-hidden-layer activation max and gradient sum of squares, output
+        range, NaN flags), or None when enable_probes is off or no pass has
+        run (TrainingStepResult.probe / read_last_split_probe)."""
+        r = _abi.ProbeResult()
+        st = lib.tmnn_cuda_last_probe(self._handle(), C.byref(r))
+        if st != _abi.OK:
+            return None
+        H = r.num_hidden_layers
+        return {"num_hidden_layers": H,
+                "has_nan_forward": bool(r.has_nan_forward),
+                "has_nan_backward": bool(r.has_nan_backward),
+                "hash_grad_l2": r.hash_grad_l2,
+                "act_max": list(r.act_max)[:H], "grad_l2": list(r.grad_l2)[:H],
+                "output_abs_max": r.output_abs_max,
+                "output_min": r.output_min}
+
     def numerics_stats(self):
         """Counters of the numerics guard (dict)."""
         s = _abi.NumericsStats()

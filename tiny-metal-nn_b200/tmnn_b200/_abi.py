@@ -23,7 +23,7 @@ BUF_HASH_WEIGHTS, BUF_MLP_WEIGHTS, BUF_GRAD_HASH, BUF_GRAD_MLP = 1, 2, 3, 4
 BUF_FUSED_WEIGHTS, BUF_FUSED_M, BUF_FUSED_V = 7, 8, 9
 BUF_HASH_GATHER, BUF_TOUCHED = 20, 21
 LOSS = {"L2": 0, "L1": 1, "Huber": 2, "Cosine": 3}
-GRAD_FIXED16, GRAD_F32 = 0, 1
+GRAD_FIXED16, GRAD_F32, GRAD_F16 = 0, 1, 2
 DTYPE_F32, DTYPE_F16 = 0, 1
 
 
@@ -54,7 +54,7 @@ class TrainCfg(C.Structure):
                 ("numerics_sample_interval", C.c_int32),
                 ("bad_step_recovery", C.c_int32),
                 ("morton_key_bits", C.c_int32),
-                ("reserved", C.c_int32 * 2)]
+                ("enable_probes", C.c_int32), ("reserved", C.c_int32)]
 
 
 class StepResult(C.Structure):
@@ -92,6 +92,14 @@ BAD_STEP = {"SignalOnly": 0, "Throw": 1, "Skip": 2, "Rollback": 3,
             "FallbackAndRetryWithSafeFamily": 4}
 RECOVERY_ACTION = {0: "None", 1: "Skipped", 2: "RolledBack",
                    3: "RetriedWithSafeFamily"}
+
+
+class ProbeResult(C.Structure):
+    _fields_ = [("num_hidden_layers", C.c_uint32),
+                ("has_nan_forward", C.c_int32), ("has_nan_backward", C.c_int32),
+                ("hash_grad_l2", C.c_float), ("act_max", C.c_float * 8),
+                ("grad_l2", C.c_float * 8), ("output_abs_max", C.c_float),
+                ("output_min", C.c_float)]
 
 
 class BufferView(C.Structure):
@@ -144,6 +152,7 @@ _SIGS = [
     ("tmnn_cuda_reset_optimizer", C.c_int, [P]),
     ("tmnn_cuda_get_step", C.c_int, [P, C.POINTER(u32)]),
     ("tmnn_cuda_get_buffer", C.c_int, [P, C.c_int32, C.POINTER(BufferView)]),
+    ("tmnn_cuda_last_probe", C.c_int, [P, C.POINTER(ProbeResult)]),
     ("tmnn_cuda_get_plan", C.c_int, [P, C.POINTER(Plan)]),
     ("tmnn_cuda_get_stream", C.c_int, [P, C.POINTER(P)]),
     ("tmnn_cuda_synchronize", C.c_int, [P]),
