@@ -749,6 +749,9 @@ def run_mlp_sweep(args, w, rank, world, local, emit):
           "sweep": pts, "clocks": ck, "gpu_launches": 20 * len(pts)})
 
 
+REF_BUDGET_S = 90.0
+
+
 def run_reference(args, w):
     """Reference arm: the reference's own code compiled here (oracle/_ref:
     its generated scalar train kernel run as C++ through the Metal shim, its
@@ -772,13 +775,14 @@ def run_reference(args, w):
     w_all = np.concatenate([table, mlp])
     m = np.zeros_like(w_all)
     v = np.zeros_like(w_all)
-    n = 2048
-    batches = [make_batch_np(w, n, 11 + i) for i in range(4)]
+    lanes = max(1, min(ro.train_lanes_max(tag), (os.cpu_count() or 1)))
     step = [0]
 
     def ref_step(pos, tgt):
+        n = pos.shape[0]
         ps, ts = ro.morton_sort(pos, tgt)
-        r = ro.train(tag, sp, w_all[:table.size], w_all[table.size:], ps, ts)
+        r = ro.train_lanes(tag, sp, w_all[:table.size], w_all[table.size:],
+                           ps, ts, lanes)
         params = ro.adam_params(w["lr"], w["lr"], 0.9, 0.99, 1e-15, 0.0, 0.0,
                                 table.size, n_mlp, step[0])
         slots = table.size // 2
@@ -792,6 +796,18 @@ def run_reference(args, w):
         step[0] += 1
         return float(r["loss_partials"].sum()) / n
 
+    # points per step: as many (a power of two, 2048 to the full batch) as
+    # keep the whole warm-up + timed run near REF_BUDGET_S seconds
+    probe = make_batch_np(w, 2048, 10)
+    ref_step(*probe)
+    t0 = time.perf_counter()
+    ref_step(*probe)
+    per_point = (time.perf_counter() - t0) / 2048
+    n = 2048
+    while n * 2 <= w["batch"] and \
+            2 * n * per_point * (args.steps + args.warmup) <= REF_BUDGET_S:
+        n *= 2
+    batches = [make_batch_np(w, n, 11 + i) for i in range(4)]
     for i in range(args.warmup):
         ref_step(*batches[i % 4])
     t0 = time.perf_counter()
@@ -808,13 +824,15 @@ def run_reference(args, w):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["desc"],
-                       "sample_points_per_step": n},
+                       "sample_points_per_step": n,
+                       "same_config": n == w["batch"]},
             "cpu_baseline": {"value": val, "unit": unit,
                              "cores": os.cpu_count(), "kind": "reference",
                              "sample": f"{args.steps} steps of {n} points through "
-                                       "the reference's generated train kernel "
-                                       "(MSL run as C++, one std::thread per "
-                                       "Metal thread), its Morton sort and its "
+                                       "the reference's generated scalar train "
+                                       "kernel (MSL run as C++, one std::thread "
+                                       f"per Metal thread, {lanes} threadgroups "
+                                       "at once), its Morton sort and its "
                                        "sparse/dense Adam kernels"},
             "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}

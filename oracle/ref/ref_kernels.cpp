@@ -4,9 +4,39 @@
 #include "tg_runner.h"
 #include <cstdint>
 
+#if defined(ROLE_TRAIN_LANES)
+// REF_LANES copies of the training kernel, one per namespace, so that each
+// lane of run_threadgroups_lanes has its own threadgroup (static) arrays.
+namespace ref_k0 {
+#include MSL_FILE
+}
+namespace ref_k1 {
+#include MSL_FILE
+}
+namespace ref_k2 {
+#include MSL_FILE
+}
+namespace ref_k3 {
+#include MSL_FILE
+}
+namespace ref_k4 {
+#include MSL_FILE
+}
+namespace ref_k5 {
+#include MSL_FILE
+}
+namespace ref_k6 {
+#include MSL_FILE
+}
+namespace ref_k7 {
+#include MSL_FILE
+}
+#define REF_LANES 8u
+#else
 namespace ref_k {
 #include MSL_FILE
 }
+#endif
 using namespace metal;
 
 extern "C" {
@@ -48,6 +78,43 @@ void tmnn_ref_train_simd(const float *pos, const float *tgt, const float *cfg,
     });
 }
 uint32_t tmnn_ref_train_simd_points_per_tg() { return TOTAL_PTS_PER_TG; }
+#elif defined(ROLE_TRAIN_LANES)
+// The reference's scalar training kernel with up to REF_LANES threadgroups
+// running at once (emulated on the host, the scalar kernel is several times
+// faster than the simdgroup-matrix one, whose matrix ops are emulated).
+// Same arguments and outputs as tmnn_ref_train; the float accumulations into
+// grad_mlp and the fixed-point hash gradients are atomic, so only the order
+// of the float sums varies.
+typedef decltype(&ref_k0::neural_sdf_train_forward_backward) train_fn;
+static const train_fn k_lane_fns[REF_LANES] = {
+    ref_k0::neural_sdf_train_forward_backward,
+    ref_k1::neural_sdf_train_forward_backward,
+    ref_k2::neural_sdf_train_forward_backward,
+    ref_k3::neural_sdf_train_forward_backward,
+    ref_k4::neural_sdf_train_forward_backward,
+    ref_k5::neural_sdf_train_forward_backward,
+    ref_k6::neural_sdf_train_forward_backward,
+    ref_k7::neural_sdf_train_forward_backward};
+uint32_t tmnn_ref_train_lanes_max() { return REF_LANES; }
+void tmnn_ref_train_lanes(const float *pos, const float *tgt, const float *cfg,
+                          const float *hash, int32_t *grad_hash,
+                          float *grad_mlp, float *loss_partials,
+                          const float *train_params, uint32_t *mask,
+                          uint32_t *summary, const float *mlp, uint32_t N,
+                          uint32_t lanes) {
+  const uint32_t tgs = (N + 127) / 128;
+  if (lanes < 1) lanes = 1;
+  if (lanes > REF_LANES) lanes = REF_LANES;
+  run_threadgroups_lanes(lanes, 128, tgs,
+                         [&](unsigned ln, unsigned tg, unsigned lid) {
+    k_lane_fns[ln](pos, tgt, cfg, hash,
+                   reinterpret_cast<atomic_int *>(grad_hash),
+                   reinterpret_cast<atomic_float *>(grad_mlp), loss_partials,
+                   train_params, reinterpret_cast<atomic_uint *>(mask),
+                   reinterpret_cast<atomic_uint *>(summary), mlp,
+                   tg * 128 + lid, tg, lid);
+  });
+}
 #elif defined(ROLE_EXTGRAD)
 void tmnn_ref_extgrad(const float *pos, const float *tgt, const float *cfg,
                       const float *hash, int32_t *grad_hash, float *grad_mlp,

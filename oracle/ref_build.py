@@ -140,11 +140,16 @@ def build(force=False):
         # reference's compiler realises it (its default there)
         probe = subprocess.run([gen, "train"] + args + ["1", "1"], check=True,
                                capture_output=True, text=True)
-        if "simd=1" in probe.stderr:
+        simd = "simd=1" in probe.stderr
+        if simd:
             roles.append(("train_simd", "ROLE_TRAIN_SIMD"))
+        # bench.py's reference arm: the scalar training kernel with
+        # threadgroups running concurrently on the host cores
+        if tag.startswith("bench_"):
+            roles.append(("train_lanes", "ROLE_TRAIN_LANES"))
         for role, define in roles:
             msl = os.path.join(OUT, f"{tag}_{role}.msl")
-            gen_role = "train" if role == "train_simd" else role
+            gen_role = "train" if role in ("train_simd", "train_lanes") else role
             flags = ["0" if role.startswith("eval") else "1"]
             if role == "train_simd":
                 flags.append("1")

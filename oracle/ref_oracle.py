@@ -118,6 +118,40 @@ def train_simd(tag, sp, table, mlp, pos, tgt, active_levels=0):
                 summary=summ)
 
 
+def train_lanes(tag, sp, table, mlp, pos, tgt, lanes=8):
+    """Runs the reference's scalar training kernel for a bench_* spec with up
+    to `lanes` emulated threadgroups at once.  Same outputs as train(); the
+    float MLP-gradient sums may differ in order."""
+    L, F, log2T, d, W, H, O = sp[:7]
+    lib = _lib(tag)
+    pos = np.ascontiguousarray(pos, np.float32)
+    N = pos.shape[0]
+    tgt = np.ascontiguousarray(tgt, np.float32)
+    cfg = _config(L, F, log2T, sp[8], sp[9], W, H, N, mlp)
+    gh = np.zeros(table.size, np.int32)
+    gm = np.zeros(mlp.size, np.float32)
+    tgs = (N + 127) // 128
+    lp = np.zeros(max(tgs, 1), np.float32)
+    tp = np.array([N, 0, 1.0, L, 0, 0, 0, 0], np.float32)
+    slots = table.size // 2 if F == 2 else table.size
+    mask = np.zeros((slots + 31) // 32, np.uint32)
+    summ = np.zeros((slots + 2047) // 2048 + 1, np.uint32)
+    table = np.ascontiguousarray(table, np.float32)
+    mlp = np.ascontiguousarray(mlp, np.float32)
+    lib.tmnn_ref_train_lanes(_p(pos), _p(tgt), _p(cfg), _p(table), _p(gh),
+                             _p(gm), _p(lp), _p(tp), _p(mask), _p(summ),
+                             _p(mlp), C.c_uint32(N), C.c_uint32(lanes))
+    return dict(loss_partials=lp, grad_hash=gh, grad_mlp=gm, mask=mask,
+                summary=summ)
+
+
+def train_lanes_max(tag):
+    """How many threadgroups train_lanes can run at once."""
+    lib = _lib(tag)
+    lib.tmnn_ref_train_lanes_max.restype = C.c_uint32
+    return int(lib.tmnn_ref_train_lanes_max())
+
+
 def mask_to_touched(mask, slots):
     bits = np.unpackbits(mask.view(np.uint8), bitorder="little")
     return bits[:slots].astype(np.uint8)

@@ -148,6 +148,23 @@ def test_simd_train_kernel_at_benchmark_shape(ref):
     assert abs(float(r["loss_partials"].sum()) - lsum) <= 1e-5 * abs(lsum)
 
 
+@pytest.mark.parametrize("tag", ["bench_sdf3d", "bench_image"])
+def test_concurrent_threadgroups_match_sequential(ref, tag):
+    """The reference arm runs several emulated threadgroups at once, each
+    lane on its own copy of the kernel's threadgroup arrays; its fixed-point
+    hash gradients, touched mask and loss partials equal the one-at-a-time
+    run, and the float MLP gradients differ only by summation order."""
+    sp = ref.spec_tuple(tag)
+    table, mlp, pos, tgt, _ = case_inputs(tag, sp, seed=5)
+    a = ref.train(tag, sp, table, mlp, pos, tgt)
+    b = ref.train_lanes(tag, sp, table, mlp, pos, tgt, lanes=4)
+    assert np.array_equal(a["grad_hash"], b["grad_hash"])
+    assert np.array_equal(a["mask"], b["mask"])
+    assert np.array_equal(a["loss_partials"], b["loss_partials"])
+    scale = max(1e-30, float(np.abs(a["grad_mlp"]).max()))
+    assert np.abs(a["grad_mlp"] - b["grad_mlp"]).max() <= 1e-5 * scale
+
+
 @pytest.mark.parametrize("tag", TAGS)
 def test_external_grad_kernel_matches_reference_golden(tag):
     g = np.load(os.path.join(GOLDEN, f"ref_{tag}.npz"))
