@@ -749,7 +749,8 @@ def run_mlp_sweep(args, w, rank, world, local, emit):
           "sweep": pts, "clocks": ck, "gpu_launches": 20 * len(pts)})
 
 
-REF_BUDGET_S = 90.0
+# seconds the reference arm's warm-up + timed steps should take
+REF_BUDGET_S = float(os.environ.get("TMNN_REF_BUDGET_S", "90"))
 
 
 def run_reference(args, w):
