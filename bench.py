@@ -486,7 +486,7 @@ def cpu_baseline(w, seconds=12.0):
     hw, mw = o.init_weights(s)
     tr = o.OracleTrainer(s, hw, mw, lr_hash=w["lr"], lr_mlp=w["lr"],
                          nthreads=0)
-    n = 1 << 14
+    n = w["batch"]  # the workload's own batch: one sample step = one step
     pos, tgt = make_batch_np(w, n, 7)
     tr.training_step(pos, tgt)  # warm-up
     steps, t0 = 0, time.perf_counter()
