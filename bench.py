@@ -849,6 +849,9 @@ def main():
     ap.add_argument("--family", default="Auto")
     ap.add_argument("--grad", default="F32")
     ap.add_argument("--no-morton", action="store_true")
+    ap.add_argument("--dp-p2p", action="store_true",
+                    help="N > 1: sharded update over NVLink peer memory "
+                         "(TMNN_DP_P2P=1) instead of NCCL collectives")
     ap.add_argument("--morton-bits", type=int, default=12,
                     help="Morton sort key bits (0: the whole code)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -859,6 +862,8 @@ def main():
                     help="mlp_sweep: one point W:H:log2N (e.g. 64:4:20)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.dp_p2p:
+        os.environ["TMNN_DP_P2P"] = "1"
     w = WORKLOADS[args.workload]
     # NCCL (torch's and the library's) print banners on stdout; stdout is
     # reserved for the single JSON line, so everything else goes to stderr
@@ -1027,6 +1032,8 @@ def main():
         "config": {"workload": args.workload, "desc": w["desc"],
                    "batch_per_gpu": B, "global_batch": B * world,
                    "parallelism": f"dp{world}", "family": plan["family"],
+                   "dp_exchange": ("peer memory" if tr.plan()["reason"].startswith(
+                       "peer-memory") else "nccl") if world > 1 else None,
                    "hash_grad_format": args.grad,
                    "morton_sort": not args.no_morton,
                    "morton_key_bits": args.morton_bits,

@@ -190,6 +190,80 @@ def test_dp_nccl_two_gpus_match_one(family, grad, sharded):
     ref.close()
 
 
+def _peer_rank(rank, world, port, q, grad):
+    import sys
+    for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),
+              os.path.join(ROOT, "oracle")):
+        sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["TMNN_DP_BUCKETS"] = "4"
+    os.environ["TMNN_DP_P2P"] = "1"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import tmnn_b200 as t
+    from _util import cuda_trainer
+    tr = cuda_trainer(**KW_FUSED, family="Tiled", grad=grad, table="F16",
+                      device=rank, cfg_extra={"dp_replicated_optimizer": -1})
+    uid = [t.dp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    tr.dp_init(uid[0], rank, world)
+    init = tr.weights()
+    losses = []
+    for pos, tgt in _data():
+        n = pos.shape[0] // world
+        losses.append(tr.training_step(np.ascontiguousarray(pos[rank * n:(rank + 1) * n]),
+                                       np.ascontiguousarray(tgt[rank * n:(rank + 1) * n])))
+    reason = tr.plan()["reason"]
+    tr.dp_sync_state()
+    q.put((rank, tr.weights(), losses, init, reason))
+    tr.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("grad", ["F32", "F16"])
+def test_dp_peer_exchange_matches_one_process(grad):
+    """The sharded update over NVLink peer memory (TMNN_DP_P2P=1: per
+    bucket, the owner sums the ranks' partial gradients with peer loads,
+    runs Adam and stores the fp16 table into every rank) against one process
+    on the whole batch, with the tolerances of the NCCL sharded path."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = min(4, torch.cuda.device_count())
+    from _util import cuda_trainer
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_peer_rank, args=(r, world, port, q, grad))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, wts, losses, init, reason = q.get(timeout=120)
+        res[r] = (wts, losses, init, reason)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][3].startswith("peer-memory"), res[0][3]
+    ref = cuda_trainer(**KW_FUSED, family="Tiled", grad=grad, table="F16")
+    ref_losses = [ref.training_step(p, t) for p, t in _data()]
+    (h0, m0), l0, (hi, mi), _ = res[0]
+    for r in range(1, world):
+        assert np.array_equal(h0, res[r][0][0]) and np.array_equal(m0, res[r][0][1])
+    hr, mr = ref.weights()
+    assert np.allclose(l0, ref_losses, rtol=1e-3 if grad == "F32" else 2e-3)
+
+    def cos(a, b):
+        a, b = a.astype(np.float64), b.astype(np.float64)
+        return a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300)
+    tol = 0.999 if grad == "F32" else 0.99
+    assert cos(h0 - hi, hr - hi) >= tol
+    assert cos(m0 - mi, mr - mi) >= tol
+    ref.close()
+
+
 def _retry_rank(rank, world, port, q):
     import sys
     for p in (ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "tiny-metal-nn_b200"),

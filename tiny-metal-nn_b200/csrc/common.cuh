@@ -83,6 +83,8 @@ struct StepStats {
   float nonfinite_upd;    // 1 when a would-be update quantity is NaN/Inf
   int32_t probed;         // 1 when the probe scanned the gradients
   int32_t gate;           // 1: Adam skips the update on an anomaly
+  int32_t exchange_err;   // 1: a rank did not reach a peer-exchange barrier
+  int32_t reserved;
 };
 
 // In-kernel training probes (ProbeResult, include/tiny-metal-nn/common.h:

@@ -44,6 +44,24 @@ void launch_numerics_probe(const AdamArgs &a, const float *w, const float *m,
 void launch_touched_from_grads(const float *g, uint8_t *touched, uint64_t slots,
                                int entry_width, bool half, int num_sms,
                                cudaStream_t st);
+// Data-parallel ranks on one node whose buffers this process maps (CUDA
+// IPC): every rank's hash-gradient buffer, fp16 gather copy of the table and
+// barrier flags (one uint32 slot per rank), indexed by rank.
+constexpr int kMaxPeers = 8;
+struct PeerTable {
+  const void *grad[kMaxPeers];
+  __half *table_h[kMaxPeers];
+  uint32_t *flags[kMaxPeers];
+};
+// Sharded update of table elements [off, off + a.hash_count) owned by this
+// rank, over peer memory: barrier, sum of the ranks' partial gradients +
+// sparse Adam on this rank's w/m/v + fp16 copy stored to every rank,
+// barrier.  Advances epoch by two (every rank runs the same sequence).
+// A barrier that times out sets *err.  Returns the kernels launched.
+int launch_peer_exchange(const AdamArgs &a, const PeerTable &pt, int rank,
+                         int world, uint64_t off, float *w, float *m, float *v,
+                         uint32_t &epoch, int32_t *err, int num_sms,
+                         cudaStream_t st);
 void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,
                      float *gm, int num_sms, cudaStream_t st);
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,

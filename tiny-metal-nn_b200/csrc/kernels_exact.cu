@@ -613,6 +613,139 @@ __global__ void __launch_bounds__(256, 4)
   if (gm) adam_mlp_range(a, w, m, v, gm, false);
 }
 
+// ------------------------------------------------------------ peer exchange
+
+// Sharded data-parallel update over NVLink peer memory, one launch per
+// bucket of levels: the rank that owns a range of the table reads every
+// rank's partial gradients of it with plain peer loads, sums them in rank
+// order, runs the sparse Adam above on the sum (implicit touch marks: a
+// nonzero sum marks its slot) and stores the updated fp16 gather copy into
+// every rank's table with plain peer stores.  This replaces a reduce-scatter,
+// the shard's Adam and an all-gather with one pass; the bytes on NVLink are
+// the reduce-scatter's reads and the all-gather's writes.  `off` is the
+// range's first element in every rank's buffers; a.hash_count its length (a
+// multiple of 4).  Gradients are not cleared here: a peer may still be
+// reading them until the closing barrier.
+// Peer loads that go to the owning GPU every time (volatile: never served
+// from a cache line filled by an earlier step).
+__device__ __forceinline__ uint4 ld_peer_v4(const void *p) {
+  uint4 r;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_peer_v2(const void *p) {
+  uint2 r;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+__global__ void __launch_bounds__(256)
+    k_peer_adam(AdamArgs a, PeerTable pt, int world, uint64_t off,
+                float *__restrict__ w, float *__restrict__ m,
+                float *__restrict__ v) {
+  if (adam_vetoed(a)) return;
+  const uint64_t n4 = a.hash_count / 4;
+  const uint64_t q0 = off / 4;
+  for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n4;
+       q += (uint64_t)gridDim.x * blockDim.x) {
+    float g[4] = {0.f, 0.f, 0.f, 0.f};
+    if (a.grad_half) {
+      uint2 r[kMaxPeers];
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k)
+        if (k < world)
+          r[k] = ld_peer_v2(reinterpret_cast<const uint2 *>(pt.grad[k]) + q0 + q);
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k) {
+        if (k >= world) break;
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&r[k].x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&r[k].y));
+        g[0] += lo.x;
+        g[1] += lo.y;
+        g[2] += hi.x;
+        g[3] += hi.y;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) g[k] *= kInvHalfGradScale;
+    } else {
+      uint4 r[kMaxPeers];
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k)
+        if (k < world)
+          r[k] = ld_peer_v4(reinterpret_cast<const uint4 *>(pt.grad[k]) + q0 + q);
+#pragma unroll
+      for (int k = 0; k < kMaxPeers; ++k) {
+        if (k >= world) break;
+        g[0] += __uint_as_float(r[k].x);
+        g[1] += __uint_as_float(r[k].y);
+        g[2] += __uint_as_float(r[k].z);
+        g[3] += __uint_as_float(r[k].w);
+      }
+    }
+    bool on[4];
+    if (a.entry_width == 2) {
+      on[0] = on[1] = g[0] != 0.f || g[1] != 0.f;
+      on[2] = on[3] = g[2] != 0.f || g[3] != 0.f;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) on[k] = g[k] != 0.f;
+    }
+    if (!(on[0] | on[1] | on[2] | on[3])) continue;
+    float4 wv = reinterpret_cast<float4 *>(w)[q];
+    float4 mv = reinterpret_cast<float4 *>(m)[q];
+    float4 vv = reinterpret_cast<float4 *>(v)[q];
+    float *pw = &wv.x, *pm = &mv.x, *pv = &vv.x;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (on[k]) adam_elem(pw[k], pm[k], pv[k], g[k], a.lr_hash, a, a.l1_hash, false);
+    reinterpret_cast<float4 *>(w)[q] = wv;
+    reinterpret_cast<float4 *>(m)[q] = mv;
+    reinterpret_cast<float4 *>(v)[q] = vv;
+    __half2 h[2] = {__floats2half2_rn(wv.x, wv.y), __floats2half2_rn(wv.z, wv.w)};
+    const uint2 hb = *reinterpret_cast<uint2 *>(h);
+#pragma unroll
+    for (int k = 0; k < kMaxPeers; ++k)
+      if (k < world) reinterpret_cast<uint2 *>(pt.table_h[k])[q0 + q] = hb;
+  }
+  // this thread's peer stores are ordered before the closing barrier's flag
+  __threadfence_system();
+}
+
+// Barrier of the ranks over peer memory: thread t announces `epoch` in slot
+// `rank` of rank t's flag array, then waits until rank t has announced it in
+// this rank's array.  Epochs only grow, so the flags are never reset.  The
+// wait gives up after about two seconds (a rank that never arrives): it sets
+// *err and returns, the context stays usable and the host reports the error.
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void k_peer_barrier(PeerTable pt, int rank, int world,
+                               uint32_t epoch, int32_t *err) {
+  const int t = threadIdx.x;
+  if (t >= world) return;
+  __threadfence_system();
+  st_release_sys(pt.flags[t] + rank, epoch);
+  const uint32_t *f = pt.flags[rank] + t;
+  const long long t0 = clock64();
+  while ((int32_t)(ld_acquire_sys(f) - epoch) < 0) {
+    if (clock64() - t0 > (1ll << 32)) {
+      atomicExch(err, 1);
+      return;
+    }
+    __nanosleep(256);
+  }
+}
+
 // ------------------------------------------------------------ numerics probe
 
 // The reference's sampled numerics probes (training_step_execution.cpp:
@@ -1073,6 +1206,22 @@ void launch_adam_mlp(const AdamArgs &a, float *w, float *m, float *v,
   if (mb)
     k_adam<<<(unsigned)mb, 256, 0, st>>>(am, w, m, v, nullptr, nullptr, gm,
                                          nullptr, nullptr);
+}
+
+int launch_peer_exchange(const AdamArgs &a, const PeerTable &pt, int rank,
+                         int world, uint64_t off, float *w, float *m, float *v,
+                         uint32_t &epoch, int32_t *err, int num_sms,
+                         cudaStream_t st) {
+  k_peer_barrier<<<1, 32, 0, st>>>(pt, rank, world, ++epoch, err);
+  const uint64_t n4 = a.hash_count / 4;
+  uint64_t blocks = (n4 + 255) / 256;
+  const uint64_t cap = (uint64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks)
+    k_peer_adam<<<(unsigned)blocks, 256, 0, st>>>(a, pt, world, off, w + off,
+                                                  m + off, v + off);
+  k_peer_barrier<<<1, 32, 0, st>>>(pt, rank, world, ++epoch, err);
+  return blocks ? 3 : 2;
 }
 
 void launch_to_half(const float *src, __half *dst, uint64_t n, int num_sms,

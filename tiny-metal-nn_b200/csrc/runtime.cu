@@ -201,6 +201,15 @@ struct tmnn_ctx {
   bool stale = false;
   // level ranges [l0, l1) whose per-rank shards the stale state follows
   std::vector<std::pair<int, int>> stale_layout;
+  // sharded update over NVLink peer memory (TMNN_DP_P2P=1, opt-in): the
+  // ranks' gradient buffers, fp16 tables and barrier flags mapped into this
+  // process; decided once, by all ranks together, at the first bucketed
+  // sharded step
+  bool p2p_decided = false, p2p = false;
+  PeerTable peers{};
+  DevBuf<uint32_t> p2p_flags;
+  std::vector<void *> p2p_opened;
+  uint32_t p2p_epoch = 0;
 
   float *hash_w() { return params.p; }
   float *mlp_w() { return params.p + hash_count; }
@@ -226,6 +235,8 @@ struct tmnn_ctx {
 
   ~tmnn_ctx() {
     if (stream) cudaStreamSynchronize(stream);
+    if (comm_stream) cudaStreamSynchronize(comm_stream);
+    for (void *q : p2p_opened) cudaIpcCloseMemHandle(q);
     if (comm) ncclCommDestroy(comm);
     if (comm_stream) {
       cudaStreamSynchronize(comm_stream);
@@ -838,6 +849,87 @@ bool buckets_shardable(const tmnn_ctx &c, const std::vector<Bucket> &bs) {
   return true;
 }
 
+// Whether every rank can run the sharded update over peer memory, decided
+// once by all ranks together (two tiny allreduces, so that no rank takes
+// the peer path alone): requested by TMNN_DP_P2P=1 (on every rank), float
+// gradients with implicit touch marks, an fp16 gather table, at most
+// kMaxPeers ranks, and the CUDA IPC mapping of every rank's gradient
+// buffer, fp16 table and barrier flags succeeding everywhere.
+int p2p_vote(tmnn_ctx &c, int mine) {
+  DevBuf<int32_t> v;
+  v.alloc(1);
+  CK(cudaMemcpyAsync(v.p, &mine, sizeof(int), cudaMemcpyHostToDevice, c.stream));
+  NK(ncclAllReduce(v.p, v.p, 1, ncclInt32, ncclMin, c.comm, c.stream));
+  int all = 0;
+  CK(cudaMemcpyAsync(&all, v.p, sizeof(int), cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  return all;
+}
+
+bool p2p_requested() {
+  const char *e = std::getenv("TMNN_DP_P2P");
+  return e && e[0] == '1';
+}
+
+// Every rank must set TMNN_DP_P2P alike: the vote below is a collective.
+void p2p_setup(tmnn_ctx &c) {
+  c.p2p = false;
+  const int want = c.world <= kMaxPeers && c.gh_float.p &&
+                   c.gather_half() && c.sparse && c.implicit_touch &&
+                   !c.gh_fixed.p;
+  if (!p2p_vote(c, want)) return;
+  struct Handles { cudaIpcMemHandle_t grad, half, flags; };
+  int ok = 1;
+  Handles mine{};
+  c.p2p_flags.alloc(kMaxPeers);
+  CK(cudaMemsetAsync(c.p2p_flags.p, 0, c.p2p_flags.bytes(), c.stream));
+  ok = cudaIpcGetMemHandle(&mine.grad, c.gh_float.p) == cudaSuccess &&
+       cudaIpcGetMemHandle(&mine.half, c.table_h.p) == cudaSuccess &&
+       cudaIpcGetMemHandle(&mine.flags, c.p2p_flags.p) == cudaSuccess;
+  cudaGetLastError();
+  std::vector<Handles> all(c.world);
+  DevBuf<uint8_t> buf;
+  buf.alloc(sizeof(Handles) * c.world);
+  CK(cudaMemcpyAsync(buf.p + sizeof(Handles) * c.rank, &mine, sizeof(Handles),
+                     cudaMemcpyHostToDevice, c.stream));
+  NK(ncclAllGather(buf.p + sizeof(Handles) * c.rank, buf.p, sizeof(Handles),
+                   ncclChar, c.comm, c.stream));
+  CK(cudaMemcpyAsync(all.data(), buf.p, buf.bytes(), cudaMemcpyDeviceToHost,
+                     c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  PeerTable pt{};
+  for (int r = 0; r < c.world && ok; ++r) {
+    if (r == c.rank) {
+      pt.grad[r] = c.gh_float.p;
+      pt.table_h[r] = c.table_h.p;
+      pt.flags[r] = c.p2p_flags.p;
+      continue;
+    }
+    void *g = nullptr, *h = nullptr, *f = nullptr;
+    ok = cudaIpcOpenMemHandle(&g, all[r].grad, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (g) c.p2p_opened.push_back(g);
+    ok = ok && cudaIpcOpenMemHandle(&h, all[r].half, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (h) c.p2p_opened.push_back(h);
+    ok = ok && cudaIpcOpenMemHandle(&f, all[r].flags, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    if (f) c.p2p_opened.push_back(f);
+    pt.grad[r] = g;
+    pt.table_h[r] = static_cast<__half *>(h);
+    pt.flags[r] = static_cast<uint32_t *>(f);
+  }
+  cudaGetLastError();
+  if (!p2p_vote(c, ok ? 1 : 0)) {
+    for (void *q : c.p2p_opened) cudaIpcCloseMemHandle(q);
+    c.p2p_opened.clear();
+    c.p2p_flags.release();
+    return;
+  }
+  c.peers = pt;
+  c.p2p_epoch = 0;
+  c.p2p = true;
+  // first, so that the plan's 128-character reason field keeps it
+  c.plan_text = "peer-memory sharded update; " + c.plan_text;
+}
+
 // One data-parallel training pass of the Tiled family, pipelined per bucket
 // of levels over two streams:
 //
@@ -859,6 +951,16 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
   const bool exch_touched = c.sparse && !c.implicit_touch;
   const uint64_t w = (uint64_t)c.entry_width;
   cudaStream_t cs = c.comm_stream;
+  if (shard && !c.p2p_decided) {
+    // only a process that asks for the peer path votes: without the
+    // variable the step runs no extra collective
+    c.p2p_decided = true;
+    if (p2p_requested()) p2p_setup(c);
+  }
+  // peer path: bucket g's sum + Adam + fp16 copy to every rank in one
+  // kernel on the comm stream right after its scatter, then the reset of
+  // the bucket's gradients once every rank has read them
+  const bool peer = shard && c.p2p;
   c.launches += tiled_encode(nd, c.params.p, c.gather_half(), pos, c.feat.p, N,
                              c.stream);
   c.launches += fused_mlp_train(c.fws, nd, c.mlp_w(), c.feat.p, tgt, nullptr,
@@ -878,6 +980,20 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
                                 b.l0, b.l1);
     CK(cudaEventRecord(c.dp_ev[1 + g], c.stream));
     CK(cudaStreamWaitEvent(cs, c.dp_ev[1 + g], 0));
+    if (peer) {
+      const uint64_t gs = b.n / c.world;
+      AdamArgs ah = adam_args(c);
+      ah.hash_count = gs;
+      ah.slots = gs / w;
+      ah.mlp_count = 0;
+      c.launches += launch_peer_exchange(ah, c.peers, c.rank, c.world,
+                                         b.e0 + gs * c.rank, c.params.p, c.m.p,
+                                         c.v.p, c.p2p_epoch,
+                                         &c.stats()->exchange_err, c.num_sms, cs);
+      CK(cudaMemsetAsync(c.ghf(b.e0), 0, b.n * c.gh_elem(), cs));
+      CK(cudaEventRecord(c.ev_comm[g], cs));
+      continue;
+    }
     NK(ncclGroupStart());
     if (shard) {
       const uint64_t gs = b.n / c.world, own = b.e0 + gs * c.rank;
@@ -917,7 +1033,7 @@ void step_overlapped(tmnn_ctx &c, const float *pos, const float *tgt,
   const bool half = c.tensor_core_family() && c.table_h.p;
   const bool per_bucket_gather =
       bs[0].n * (half ? 2 : 4) >= (32ull << 20);  // bytes of a bucket's table
-  for (size_t g = 0; g < bs.size(); ++g) {
+  for (size_t g = 0; g < bs.size() && !peer; ++g) {
     const Bucket &b = bs[g];
     CK(cudaStreamWaitEvent(c.stream, c.ev_comm[g], 0));
     if (prof && g + 1 == bs.size()) CK(cudaEventRecord(c.ev[3], c.stream));
@@ -1277,6 +1393,10 @@ struct StepReport {
 };
 
 StepReport read_report(const StepStats &h, uint64_t global_n) {
+  if (h.exchange_err)
+    throw std::runtime_error(
+        "data-parallel exchange: a rank did not reach the peer-memory "
+        "barrier within its wait bound; the step's update is incomplete");
   StepReport r;
   // finalize_async_step: mean_loss = total / float(batch_N)
   // (parameter_store.cpp:303-322)
