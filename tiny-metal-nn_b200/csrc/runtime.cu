@@ -2398,6 +2398,11 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
     }
     if (c->stale) throw std::invalid_argument(
         "dp_init: call tmnn_cuda_dp_sync_state before re-initialising");
+    // a new communicator decides the peer-memory path afresh
+    if (c->comm_stream) CK(cudaStreamSynchronize(c->comm_stream));
+    for (void *q : c->p2p_opened) cudaIpcCloseMemHandle(q);
+    c->p2p_opened.clear();
+    c->p2p_decided = c->p2p = false;
     c->rank = rank;
     c->world = world;
     if (world > 1) {
