@@ -2402,6 +2402,7 @@ tmnn_status tmnn_cuda_dp_init(tmnn_ctx *c, const uint8_t unique_id[128],
     if (c->comm_stream) CK(cudaStreamSynchronize(c->comm_stream));
     for (void *q : c->p2p_opened) cudaIpcCloseMemHandle(q);
     c->p2p_opened.clear();
+    if (c->p2p) c->plan_text.erase(0, c->plan_text.find("; ") + 2);
     c->p2p_decided = c->p2p = false;
     c->rank = rank;
     c->world = world;
